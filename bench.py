@@ -1,0 +1,341 @@
+"""Benchmark: fwd+bwd of causal sliding-window + sink + GQA attention on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg2_gptoss_swa]
+    python bench.py --impl reference ...      # the CPU reference arm (oracle port, host cores)
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Metric: effective TFLOP/s of fwd+bwd counting only useful (window + sink) FLOPs
+(14 * D per visible (query, key) pair), whole job over all ranks.  Multi-GPU runs are weak
+scaling: every rank owns its own batch shard of the workload (independent (batch, KV-head)
+units, no collective on the data path); the barrier and the max-over-ranks device time are
+the only cross-rank traffic.
+
+Prints ONE JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+PKG = importlib.import_module("flashattention-gpt-oss-finetuning_b200")
+wl = importlib.import_module("flashattention-gpt-oss-finetuning_b200.workloads")
+plan_mod = importlib.import_module("flashattention-gpt-oss-finetuning_b200.plan")
+
+METRIC = "fwd+bwd effective TFLOP/s (window+sink FLOPs only)"
+UNIT = "TFLOP/s"
+L2_BYTES = 126 * 2**20
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return j["hbm_gbs"], j["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------------------
+# Algorithmic work per kernel (per launch over the whole problem)
+# ---------------------------------------------------------------------------------------
+
+def kernel_work(w: wl.Workload, batch: int):
+    e = 2
+    pairs = batch * w.n_q_heads * wl.visible_pairs_per_head(w.seq_len, w.window_size, w.sink_size)
+    d = w.head_dim
+    qbytes = batch * w.n_q_heads * w.seq_len * d * e
+    kbytes = batch * w.n_kv_heads * w.seq_len * d * e
+    rows = batch * w.n_q_heads * w.seq_len * 4
+    return {
+        "fwd": dict(flops=4 * d * pairs, bytes=qbytes + 2 * kbytes + qbytes + rows),
+        "bwd_preprocess": dict(flops=2 * qbytes // e, bytes=2 * qbytes + rows),
+        "bwd_dkdv": dict(flops=8 * d * pairs, bytes=2 * qbytes + 2 * kbytes + 2 * rows + 2 * kbytes),
+        "bwd_dq": dict(flops=6 * d * pairs, bytes=2 * qbytes + 2 * kbytes + 2 * rows + qbytes),
+    }
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for n, val in zip(names, parts[5:9]):
+                    if val.lower().startswith("active"):
+                        reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------
+# CPU arm: the oracle port of the reference's naive attention on the host cores
+# ---------------------------------------------------------------------------------------
+
+def cpu_sample_time(w: wl.Workload, steps: int, warmup: int):
+    """Time fwd+bwd of the oracle on one (batch, query head) slice of ``w`` per step."""
+    from oracle import swa_oracle as orc   # the checker / CPU baseline only
+    torch.set_num_threads(os.cpu_count() or 1)
+    sample = w.replace(batch=1, n_q_heads=1, n_kv_heads=1)
+    q, k, v, do = (t.float() for t in wl.make_inputs(w.replace(batch=1), kv_heads=[0])[:4])
+    q, do = q[:, :1].contiguous(), do[:, :1].contiguous()
+    for _ in range(warmup):
+        orc.backward(q, k, v, do, w.window_size, w.sink_size, compute_dtype=torch.float32)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        orc.backward(q, k, v, do, w.window_size, w.sink_size, compute_dtype=torch.float32)
+        times.append(time.perf_counter() - t0)
+    flops = wl.useful_flops(sample)
+    t = statistics.median(times)
+    return {
+        "value": flops / t / 1e12, "unit": UNIT, "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": (f"oracle (fp32 torch-CPU restatement of pytorch_naive_attention + its "
+                   f"gradient) on 1 of {w.batch * w.n_q_heads} (batch, query head) slices of "
+                   f"{w.name}, fwd+bwd, median of {steps}"),
+        "ms_per_sample": t * 1e3,
+    }
+
+
+def run_reference(args, w, rank, world):
+    if rank != 0:
+        return
+    steps, warmup = max(1, min(args.steps, 10)), max(1, min(args.warmup, 3))
+    cb = cpu_sample_time(w, steps, warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT,
+        "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
+        "ms_per_step": cb["ms_per_sample"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded randn, BASELINE shapes)",
+        "config": dict(w.describe(), sample="1 (batch, query head) slice per step"),
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------------------
+
+def device_timed(w, dev, rank, steps, warmup):
+    q, k, v, do = wl.make_inputs(w.replace(seed=w.seed + 1000 * rank), device=dev)
+    plan = plan_mod.SwaPlan(q, k, v, w.window_size, w.sink_size, None, dout=do)
+    stream = torch.cuda.current_stream(dev)
+    phases = ("fwd", "bwd_preprocess", "bwd_dkdv", "bwd_dq")
+    fns = (plan.fwd, plan.bwd_preprocess, plan.bwd_dkdv, plan.bwd_dq)
+    for _ in range(warmup):
+        plan.step(stream)
+    torch.cuda.synchronize(dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(fns) + 1)]
+           for _ in range(steps)]
+    launches0 = plan.launches
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for s in range(steps):
+        evs[s][0].record(stream)
+        for i, fn in enumerate(fns):
+            fn(stream)
+            evs[s][i + 1].record(stream)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    total_ms = start.elapsed_time(end)
+    per_phase = {p: sum(evs[s][i].elapsed_time(evs[s][i + 1]) for s in range(steps)) / steps
+                 for i, p in enumerate(phases)}
+    return total_ms, per_phase, plan.launches - launches0
+
+
+def e2e_timed(w, dev, rank, steps, warmup):
+    """Public API (autograd Function) with pinned host buffers, copies inside the timed region."""
+    q, k, v, do = (t.pin_memory() for t in wl.make_inputs(w.replace(seed=w.seed + 1000 * rank)))
+    outs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (q, q, k, v)]
+    stream = torch.cuda.current_stream(dev)
+    h2d = sum(t.numel() * t.element_size() for t in (q, k, v, do))
+    d2h = sum(t.numel() * t.element_size() for t in outs)
+
+    def step():
+        qd, kd, vd, dod = (t.to(dev, non_blocking=True) for t in (q, k, v, do))
+        qd.requires_grad_(); kd.requires_grad_(); vd.requires_grad_()
+        o = PKG.flash_swda_with_sink(qd, kd, vd, w.window_size, w.sink_size)
+        o.backward(dod)
+        for dst, src in zip(outs, (o, qd.grad, kd.grad, vd.grad)):
+            dst.copy_(src.detach(), non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    return a.elapsed_time(b), h2d, d2h
+
+
+def max_over_ranks(x: float, dev) -> float:
+    if not torch.distributed.is_initialized():
+        return x
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_ours(args, w, rank, world, local_rank):
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    hbm_peak, tf_peak, peak_kind = _peaks()
+    clocks = ClockSampler(local_rank) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    total_ms, per_phase, launches = device_timed(w, dev, rank, args.steps, args.warmup)
+    clk = clocks.stop() if clocks else None
+    total_ms = max_over_ranks(total_ms, dev)
+    ms = total_ms / args.steps
+    flops_job = wl.useful_flops(w) * world
+    value = flops_job / (ms * 1e-3) / 1e12
+
+    e2e = None
+    if not args.no_e2e:
+        e_steps = max(3, min(args.steps, 10))
+        e_ms, h2d, d2h = e2e_timed(w, dev, rank, e_steps, max(3, min(args.warmup, 3)))
+        e_ms = max_over_ranks(e_ms, dev) / e_steps
+        e2e = {"value": flops_job / (e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e_ms,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "path": "flash_swda_with_sink autograd, pinned host in/out"}
+
+    if rank != 0:
+        return
+    work = kernel_work(w, w.batch)
+    dom = max(per_phase, key=per_phase.get)
+    kw = work[dom]
+    t_s = per_phase[dom] * 1e-3
+    t_tensor = kw["flops"] / (tf_peak * 1e12)
+    t_hbm = kw["bytes"] / (hbm_peak * 1e9)
+    if t_tensor >= t_hbm:
+        roof = {"bound": "tensor", "achieved": kw["flops"] / t_s / 1e12, "peak": tf_peak,
+                "unit": "TFLOP/s"}
+    else:
+        roof = {"bound": "hbm", "achieved": kw["bytes"] / t_s / 1e9, "peak": hbm_peak,
+                "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof.update(kernel=dom, peak_source=f"MEASURED_PEAKS.json burst ({peak_kind})",
+                algorithmic_flops=kw["flops"], algorithmic_bytes=kw["bytes"],
+                kernel_ms=per_phase[dom], traffic=TRAFFIC.get((w.name, dom)),
+                tensor_frac=(kw["flops"] / t_s / 1e12) / tf_peak,
+                hbm_frac=(kw["bytes"] / t_s / 1e9) / hbm_peak)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": str(w.dtype).replace("torch.", "").replace("bfloat16", "bf16").replace("float16", "f16"),
+        "data": "synthetic (seeded randn of the workload's shape; no dataset)",
+        "config": dict(w.describe(), global_batch=w.batch * world, parallelism=f"dp{world} by (batch, kv_head) units",
+                       l2="inputs larger than L2 (q, dO 134 MB each + k, v, o, grads)"),
+        "phase_ms": per_phase,
+        "gpu_launches": launches,
+        "roofline": roof,
+        "clocks": clk,
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        cb = cpu_sample_time(w, 3, 1)
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    print(json.dumps(line), flush=True)
+
+
+# DRAM bytes (read + write) per launch from one ncu capture, keyed by (workload, kernel).
+TRAFFIC: dict = {}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="cfg2_gptoss_swa", choices=sorted(wl.CONFIGS))
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    w = wl.CONFIGS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, w, rank, world)
+        return
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, w, rank, world, local_rank)
+    finally:
+        if torch.distributed.is_initialized():
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

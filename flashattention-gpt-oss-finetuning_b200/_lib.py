@@ -1,0 +1,128 @@
+"""ctypes binding of ``lib/libswa_attn.so`` (declared in ``include/swa_attn.h``).
+
+The library is the only compute path: when it is missing, :func:`lib` raises, so no call can
+silently fall back to CPU or eager PyTorch arithmetic.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG_DIR, "lib", "libswa_attn.so")
+
+SWA_OK = 0
+SWA_ERR_INVALID_ARG = 1
+SWA_ERR_UNSUPPORTED = 2
+SWA_ERR_LAUNCH = 3
+SWA_ERR_DEVICE_TIMEOUT = 4
+SWA_ERR_WORKSPACE = 5
+
+SWA_F16 = 0
+SWA_BF16 = 1
+
+# Every extern "C" symbol include/swa_attn.h declares.
+EXPORTED_SYMBOLS = (
+    "swa_fwd", "swa_bwd", "swa_bwd_preprocess", "swa_bwd_dq", "swa_bwd_dkdv",
+    "swa_bwd_workspace_size", "swa_status_string", "swa_last_cuda_error", "swa_version",
+)
+
+
+class SwaProblem(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int32), ("n_q_heads", ctypes.c_int32), ("n_kv_heads", ctypes.c_int32),
+        ("seq_len", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("window_size", ctypes.c_int32),
+        ("sink_size", ctypes.c_int32), ("dtype", ctypes.c_int32), ("softmax_scale", ctypes.c_float),
+    ]
+
+
+class SwaTensor(ctypes.Structure):
+    _fields_ = [("ptr", ctypes.c_void_p), ("stride_b", ctypes.c_int64),
+                ("stride_h", ctypes.c_int64), ("stride_l", ctypes.c_int64)]
+
+
+class SwaFwdArgs(ctypes.Structure):
+    _fields_ = [("p", SwaProblem), ("q", SwaTensor), ("k", SwaTensor), ("v", SwaTensor),
+                ("o", SwaTensor), ("lse", ctypes.c_void_p)]
+
+
+class SwaBwdArgs(ctypes.Structure):
+    _fields_ = [("p", SwaProblem), ("q", SwaTensor), ("k", SwaTensor), ("v", SwaTensor),
+                ("o", SwaTensor), ("dout", SwaTensor), ("lse", ctypes.c_void_p),
+                ("dq", SwaTensor), ("dk", SwaTensor), ("dv", SwaTensor),
+                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t)]
+
+
+class SwaError(RuntimeError):
+    """A non-zero SwaStatus from the library."""
+
+    def __init__(self, status: int, where: str, detail: str = ""):
+        self.status = status
+        msg = f"{where}: {STATUS_NAMES.get(status, 'unknown status')} (status {status})"
+        if detail:
+            msg += f": {detail}"
+        super().__init__(msg)
+
+
+class SwaDeviceTimeout(SwaError):
+    """An on-device bounded wait gave up (SWA_ERR_DEVICE_TIMEOUT)."""
+
+
+STATUS_NAMES = {
+    SWA_OK: "ok", SWA_ERR_INVALID_ARG: "invalid argument",
+    SWA_ERR_UNSUPPORTED: "unsupported shape, dtype or layout", SWA_ERR_LAUNCH: "CUDA launch failed",
+    SWA_ERR_DEVICE_TIMEOUT: "on-device wait timed out",
+    SWA_ERR_WORKSPACE: "workspace missing, misaligned or too small",
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def _declare(l):
+    P = ctypes.POINTER
+    l.swa_fwd.argtypes = [P(SwaFwdArgs), ctypes.c_void_p]
+    for name in ("swa_bwd", "swa_bwd_preprocess", "swa_bwd_dq", "swa_bwd_dkdv"):
+        getattr(l, name).argtypes = [P(SwaBwdArgs), ctypes.c_void_p]
+        getattr(l, name).restype = ctypes.c_int
+    l.swa_fwd.restype = ctypes.c_int
+    l.swa_bwd_workspace_size.argtypes = [P(SwaProblem)]
+    l.swa_bwd_workspace_size.restype = ctypes.c_size_t
+    l.swa_status_string.argtypes = [ctypes.c_int]
+    l.swa_status_string.restype = ctypes.c_char_p
+    l.swa_last_cuda_error.argtypes = []
+    l.swa_last_cuda_error.restype = ctypes.c_char_p
+    l.swa_version.argtypes = []
+    l.swa_version.restype = ctypes.c_int
+
+
+def lib_path() -> str:
+    return LIB_PATH
+
+
+def lib():
+    """Load (once) and return the C-ABI library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise ImportError(
+                        f"{LIB_PATH} is missing: build it with "
+                        "`python flashattention-gpt-oss-finetuning_b200/build.py` "
+                        "(there is no CPU or eager fallback)")
+                l = ctypes.CDLL(LIB_PATH)
+                _declare(l)
+                _lib = l
+    return _lib
+
+
+def check(status: int, where: str):
+    if status == SWA_OK:
+        return
+    detail = ""
+    if status == SWA_ERR_LAUNCH:
+        detail = lib().swa_last_cuda_error().decode()
+    cls = SwaDeviceTimeout if status == SWA_ERR_DEVICE_TIMEOUT else SwaError
+    raise cls(status, where, detail)

@@ -1,0 +1,197 @@
+// swa_api.cu -- the extern "C" entry points declared in include/swa_attn.h: argument
+// validation (the checks of flash_attention_gpt_oss.py:343-354 plus the layout
+// requirements of these kernels), dtype/head-dim dispatch and error reporting.
+#include <string.h>
+
+#include <string>
+
+#include "swa_common.cuh"
+#include "swa_params.cuh"
+
+namespace swa {
+template <typename T, int D> cudaError_t launch_fwd_mma(const FwdParams&, cudaStream_t);
+template <typename T, int D> cudaError_t launch_bwd_preprocess(const BwdParams&, cudaStream_t);
+template <typename T, int D> cudaError_t launch_bwd_dq_mma(const BwdParams&, cudaStream_t);
+template <typename T, int D> cudaError_t launch_bwd_dkdv_mma(const BwdParams&, cudaStream_t);
+}  // namespace swa
+
+namespace {
+
+thread_local std::string g_last_cuda_error;
+
+int record(cudaError_t e) {
+  if (e == cudaSuccess) return SWA_OK;
+  g_last_cuda_error = cudaGetErrorString(e);
+  return SWA_ERR_LAUNCH;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_problem(const SwaProblem& p) {
+  if (p.batch < 0 || p.n_q_heads <= 0 || p.n_kv_heads <= 0 || p.seq_len < 0 || p.head_dim <= 0)
+    return SWA_ERR_INVALID_ARG;
+  if (p.n_q_heads % p.n_kv_heads != 0) return SWA_ERR_INVALID_ARG;   // :354
+  if (p.head_dim > 128) return SWA_ERR_INVALID_ARG;                  // :353
+  if (p.sink_size < 0) return SWA_ERR_INVALID_ARG;
+  if (!(p.softmax_scale == p.softmax_scale)) return SWA_ERR_INVALID_ARG;  // NaN scale
+  if (p.dtype != SWA_F16 && p.dtype != SWA_BF16) return SWA_ERR_UNSUPPORTED;
+  switch (p.head_dim) {
+    case 16: case 32: case 64: case 128: break;
+    default: return SWA_ERR_UNSUPPORTED;
+  }
+  return SWA_OK;
+}
+
+// Every tensor needs 16-byte aligned rows: base pointer and all three strides.
+int check_tensor(const SwaTensor& t, bool need_ptr) {
+  if (!t.ptr) return need_ptr ? SWA_ERR_INVALID_ARG : SWA_OK;
+  if (!aligned16(t.ptr)) return SWA_ERR_UNSUPPORTED;
+  if ((t.stride_b % 8) || (t.stride_h % 8) || (t.stride_l % 8)) return SWA_ERR_UNSUPPORTED;
+  if (t.stride_b < 0 || t.stride_h < 0 || t.stride_l < 0) return SWA_ERR_UNSUPPORTED;
+  return SWA_OK;
+}
+
+swa::Strides strides(const SwaTensor& t) { return {t.stride_b, t.stride_h, t.stride_l}; }
+
+int effective_window(int w) { return w < 0 ? 0 : w; }
+
+template <template <typename, int> class F, typename P>
+int dispatch(const SwaProblem& pr, const P& kp, cudaStream_t st) {
+  cudaError_t e = cudaErrorInvalidValue;
+#define SWA_D(T)                                          \
+  switch (pr.head_dim) {                                  \
+    case 16: e = F<T, 16>::run(kp, st); break;            \
+    case 32: e = F<T, 32>::run(kp, st); break;            \
+    case 64: e = F<T, 64>::run(kp, st); break;            \
+    case 128: e = F<T, 128>::run(kp, st); break;          \
+    default: return SWA_ERR_UNSUPPORTED;                  \
+  }
+  if (pr.dtype == SWA_F16) {
+    SWA_D(__half)
+  } else {
+    SWA_D(__nv_bfloat16)
+  }
+#undef SWA_D
+  return record(e);
+}
+
+template <typename T, int D> struct Fwd {
+  static cudaError_t run(const swa::FwdParams& p, cudaStream_t s) { return swa::launch_fwd_mma<T, D>(p, s); }
+};
+template <typename T, int D> struct Pre {
+  static cudaError_t run(const swa::BwdParams& p, cudaStream_t s) { return swa::launch_bwd_preprocess<T, D>(p, s); }
+};
+template <typename T, int D> struct Dq {
+  static cudaError_t run(const swa::BwdParams& p, cudaStream_t s) { return swa::launch_bwd_dq_mma<T, D>(p, s); }
+};
+template <typename T, int D> struct Dkdv {
+  static cudaError_t run(const swa::BwdParams& p, cudaStream_t s) { return swa::launch_bwd_dkdv_mma<T, D>(p, s); }
+};
+
+size_t delta_bytes(const SwaProblem& p) {
+  size_t n = (size_t)p.batch * p.n_q_heads * p.seq_len * sizeof(float);
+  return (n + 255) & ~(size_t)255;
+}
+
+int build_bwd(const SwaBwdArgs* a, swa::BwdParams* kp) {
+  if (!a) return SWA_ERR_INVALID_ARG;
+  int st = check_problem(a->p);
+  if (st) return st;
+  const SwaTensor* need[] = {&a->q, &a->k, &a->v, &a->o, &a->dout, &a->dq, &a->dk, &a->dv};
+  const bool empty = (int64_t)a->p.batch * a->p.seq_len == 0;
+  for (const SwaTensor* t : need)
+    if ((st = check_tensor(*t, !empty))) return st;
+  if (!empty && !a->lse) return SWA_ERR_INVALID_ARG;
+  if (!empty && (!a->workspace || a->workspace_bytes < swa_bwd_workspace_size(&a->p)))
+    return SWA_ERR_WORKSPACE;
+  if (!empty && (reinterpret_cast<uintptr_t>(a->workspace) & 255u)) return SWA_ERR_WORKSPACE;
+  const SwaProblem& p = a->p;
+  kp->q = a->q.ptr; kp->k = a->k.ptr; kp->v = a->v.ptr; kp->o = a->o.ptr; kp->dout = a->dout.ptr;
+  kp->lse = a->lse;
+  kp->delta = static_cast<float*>(a->workspace);
+  kp->dq = a->dq.ptr; kp->dk = a->dk.ptr; kp->dv = a->dv.ptr;
+  kp->sq = strides(a->q); kp->sk = strides(a->k); kp->sv = strides(a->v); kp->so = strides(a->o);
+  kp->sdo = strides(a->dout); kp->sdq = strides(a->dq); kp->sdk = strides(a->dk); kp->sdv = strides(a->dv);
+  kp->B = p.batch; kp->Hq = p.n_q_heads; kp->Hkv = p.n_kv_heads; kp->L = p.seq_len;
+  kp->W = effective_window(p.window_size); kp->S = p.sink_size;
+  kp->scale = p.softmax_scale;
+  kp->scale_log2 = p.softmax_scale * swa::kLog2e;
+  return SWA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int swa_version(void) { return 100; }
+
+const char* swa_status_string(int s) {
+  switch (s) {
+    case SWA_OK: return "ok";
+    case SWA_ERR_INVALID_ARG: return "invalid argument";
+    case SWA_ERR_UNSUPPORTED: return "unsupported shape, dtype or layout";
+    case SWA_ERR_LAUNCH: return "CUDA launch failed";
+    case SWA_ERR_DEVICE_TIMEOUT: return "on-device wait timed out";
+    case SWA_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+    default: return "unknown status";
+  }
+}
+
+const char* swa_last_cuda_error(void) { return g_last_cuda_error.c_str(); }
+
+size_t swa_bwd_workspace_size(const SwaProblem* p) {
+  if (!p) return 0;
+  return delta_bytes(*p);
+}
+
+int swa_fwd(const SwaFwdArgs* a, void* stream) {
+  if (!a) return SWA_ERR_INVALID_ARG;
+  int st = check_problem(a->p);
+  if (st) return st;
+  const bool empty = (int64_t)a->p.batch * a->p.seq_len == 0;
+  const SwaTensor* need[] = {&a->q, &a->k, &a->v, &a->o};
+  for (const SwaTensor* t : need)
+    if ((st = check_tensor(*t, !empty))) return st;
+  if (empty) return SWA_OK;
+  if (!a->lse) return SWA_ERR_INVALID_ARG;
+  swa::FwdParams kp;
+  kp.q = a->q.ptr; kp.k = a->k.ptr; kp.v = a->v.ptr; kp.o = a->o.ptr; kp.lse = a->lse;
+  kp.sq = strides(a->q); kp.sk = strides(a->k); kp.sv = strides(a->v); kp.so = strides(a->o);
+  kp.B = a->p.batch; kp.Hq = a->p.n_q_heads; kp.Hkv = a->p.n_kv_heads; kp.L = a->p.seq_len;
+  kp.W = effective_window(a->p.window_size); kp.S = a->p.sink_size;
+  kp.scale_log2 = a->p.softmax_scale * swa::kLog2e;
+  return dispatch<Fwd>(a->p, kp, static_cast<cudaStream_t>(stream));
+}
+
+int swa_bwd_preprocess(const SwaBwdArgs* a, void* stream) {
+  swa::BwdParams kp;
+  int st = build_bwd(a, &kp);
+  if (st || (int64_t)a->p.batch * a->p.seq_len == 0) return st;
+  return dispatch<Pre>(a->p, kp, static_cast<cudaStream_t>(stream));
+}
+
+int swa_bwd_dq(const SwaBwdArgs* a, void* stream) {
+  swa::BwdParams kp;
+  int st = build_bwd(a, &kp);
+  if (st || (int64_t)a->p.batch * a->p.seq_len == 0) return st;
+  return dispatch<Dq>(a->p, kp, static_cast<cudaStream_t>(stream));
+}
+
+int swa_bwd_dkdv(const SwaBwdArgs* a, void* stream) {
+  swa::BwdParams kp;
+  int st = build_bwd(a, &kp);
+  if (st || (int64_t)a->p.batch * a->p.seq_len == 0) return st;
+  return dispatch<Dkdv>(a->p, kp, static_cast<cudaStream_t>(stream));
+}
+
+int swa_bwd(const SwaBwdArgs* a, void* stream) {
+  swa::BwdParams kp;
+  int st = build_bwd(a, &kp);
+  if (st || (int64_t)a->p.batch * a->p.seq_len == 0) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((st = dispatch<Pre>(a->p, kp, s))) return st;
+  if ((st = dispatch<Dkdv>(a->p, kp, s))) return st;
+  return dispatch<Dq>(a->p, kp, s);
+}
+
+}  // extern "C"

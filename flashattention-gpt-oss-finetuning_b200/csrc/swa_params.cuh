@@ -1,0 +1,39 @@
+// swa_params.cuh -- kernel parameter blocks (plain values, passed by value to kernels).
+#pragma once
+#include <stdint.h>
+
+namespace swa {
+
+struct Strides {
+  int64_t b, h, l;
+};
+
+struct FwdParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse;  // [B, Hq, L] contiguous, log2 domain
+  Strides sq, sk, sv, so;
+  int B, Hq, Hkv, L, W, S;
+  float scale_log2;  // softmax_scale * log2(e)
+};
+
+struct BwdParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;
+  const void* dout;
+  const float* lse;  // [B, Hq, L] log2 domain
+  float* delta;      // [B, Hq, L] workspace
+  void* dq;
+  void* dk;
+  void* dv;
+  Strides sq, sk, sv, so, sdo, sdq, sdk, sdv;
+  int B, Hq, Hkv, L, W, S;
+  float scale;       // softmax_scale
+  float scale_log2;  // softmax_scale * log2(e)
+};
+
+}  // namespace swa

@@ -1,0 +1,159 @@
+"""Drop-in replacement for the reference module ``flash_attention_gpt_oss.py``.
+
+Same public names, signatures, argument meaning and error behaviour as the reference
+(junhown3/FlashAttention-GPT-OSS-finetuning, flash_attention_gpt_oss.py:340-438):
+
+    FlashSWDAWithSink.apply(q, k, v, window_size, sink_size, is_causal=True, softmax_scale=None)
+    flash_swda_with_sink(q, k, v, window_size, sink_size=0, is_causal=True, scale=None)
+
+``q: [B, Hq, L, D]``, ``k, v: [B, Hkv, L, D]`` (fp16 or bf16, on a CUDA device), output
+``[B, Hq, L, D]``.  Query head ``h`` reads KV head ``h // (Hq // Hkv)``; key ``j`` is visible
+to query ``i`` iff ``j <= i`` and (``i - j < window_size`` or ``j < sink_size``).
+
+Underneath, the reference's Triton kernels are replaced by the C-ABI library
+``lib/libswa_attn.so`` (sm_100a CUDA kernels); this module only validates, allocates with the
+torch caching allocator and passes raw pointers, element strides and the current CUDA stream.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.float16: _lib.SWA_F16, torch.bfloat16: _lib.SWA_BF16}
+_KERNEL_HEAD_DIMS = (16, 32, 64, 128)
+
+
+def _kernel_head_dim(d: int) -> int:
+    for k in _KERNEL_HEAD_DIMS:
+        if d <= k:
+            return k
+    raise AssertionError("Head dimension must be less than or equal to 128")
+
+
+def _prep(t: torch.Tensor, d_kernel: int) -> torch.Tensor:
+    """Zero-pad the head dim to a kernel size and make rows 16-byte aligned if needed."""
+    if t.shape[-1] != d_kernel:
+        t = torch.nn.functional.pad(t, (0, d_kernel - t.shape[-1]))
+    ok = (t.stride(-1) == 1 and all(s % 8 == 0 for s in t.stride()[:3])
+          and t.data_ptr() % 16 == 0)
+    return t if ok else t.contiguous()
+
+
+def _tensor(t: Optional[torch.Tensor]) -> _lib.SwaTensor:
+    if t is None:
+        return _lib.SwaTensor(None, 0, 0, 0)
+    s = t.stride()
+    return _lib.SwaTensor(t.data_ptr(), s[0], s[1], s[2])
+
+
+def _problem(q, k, window_size, sink_size, scale, d_kernel) -> _lib.SwaProblem:
+    b, hq, l, _ = q.shape
+    w = int(window_size)
+    w = max(-1, min(w, 2**31 - 1))
+    return _lib.SwaProblem(b, hq, k.shape[1], l, d_kernel, w, int(sink_size), _DTYPES[q.dtype],
+                           float(scale))
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _validate(q, k, v, is_causal):
+    """The reference's checks (flash_attention_gpt_oss.py:343-354), same exception type."""
+    assert is_causal, "Currently, only causal attention is supported"
+    assert q.dim() == 4 and k.dim() == 4 and v.dim() == 4, "q, k, v must be [B, H, L, D]"
+    assert q.shape[0] == v.shape[0] and q.shape[2] == v.shape[2] and q.shape[3] == v.shape[3], \
+        "Query and Value shapes must be compatible except for num_heads"
+    assert k.shape == v.shape, "Key and Value shapes must be the same"
+    assert q.shape[-1] <= 128, "Head dimension must be less than or equal to 128"
+    assert q.shape[1] % k.shape[1] == 0, \
+        "Number of query heads must be divisible by number of K/V heads"
+    if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError(f"q, k, v must share one dtype in (float16, bfloat16); got "
+                        f"{q.dtype}, {k.dtype}, {v.dtype}")
+    if not (q.is_cuda and k.device == q.device and v.device == q.device):
+        raise ValueError("q, k, v must be on the same CUDA device")
+
+
+def swa_forward(q, k, v, window_size: int, sink_size: int = 0,
+                softmax_scale: Optional[float] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Forward only: returns ``(o, lse)`` where ``lse`` is the base-2 row log-sum-exp
+    ([B, Hq, L] fp32, -inf for a row that sees no key)."""
+    _validate(q, k, v, True)
+    d = q.shape[-1]
+    if softmax_scale is None:
+        softmax_scale = 1.0 / math.sqrt(d)
+    dk_ = _kernel_head_dim(d)
+    qp, kp, vp = (_prep(t, dk_) for t in (q, k, v))
+    b, hq, l, _ = q.shape
+    o = torch.empty((b, hq, l, dk_), device=q.device, dtype=q.dtype)
+    lse = torch.empty((b, hq, l), device=q.device, dtype=torch.float32)
+    args = _lib.SwaFwdArgs(_problem(q, k, window_size, sink_size, softmax_scale, dk_),
+                           _tensor(qp), _tensor(kp), _tensor(vp), _tensor(o), lse.data_ptr())
+    with torch.cuda.device(q.device):
+        _lib.check(_lib.lib().swa_fwd(ctypes.byref(args), _stream(q.device)), "swa_fwd")
+    if dk_ != d:
+        o = o[..., :d]
+    return o, lse
+
+
+def swa_backward(q, k, v, o, lse, do, window_size: int, sink_size: int = 0,
+                 softmax_scale: Optional[float] = None):
+    """Backward: returns ``(dq, dk, dv)`` in the input dtype (deterministic)."""
+    d = q.shape[-1]
+    if softmax_scale is None:
+        softmax_scale = 1.0 / math.sqrt(d)
+    dk_ = _kernel_head_dim(d)
+    if do.dtype != q.dtype:
+        do = do.to(q.dtype)
+    qp, kp, vp, op, dop = (_prep(t, dk_) for t in (q, k, v, o, do))
+    b, hq, l, _ = q.shape
+    dq = torch.empty((b, hq, l, dk_), device=q.device, dtype=q.dtype)
+    dk = torch.empty((b, k.shape[1], l, dk_), device=q.device, dtype=q.dtype)
+    dv = torch.empty_like(dk)
+    prob = _problem(q, k, window_size, sink_size, softmax_scale, dk_)
+    lib = _lib.lib()
+    ws_bytes = lib.swa_bwd_workspace_size(ctypes.byref(prob))
+    ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
+    args = _lib.SwaBwdArgs(prob, _tensor(qp), _tensor(kp), _tensor(vp), _tensor(op), _tensor(dop),
+                           lse.data_ptr(), _tensor(dq), _tensor(dk), _tensor(dv),
+                           ws.data_ptr(), ws_bytes)
+    with torch.cuda.device(q.device):
+        _lib.check(lib.swa_bwd(ctypes.byref(args), _stream(q.device)), "swa_bwd")
+    if dk_ != d:
+        dq, dk, dv = dq[..., :d], dk[..., :d], dv[..., :d]
+    return dq, dk, dv
+
+
+class FlashSWDAWithSink(torch.autograd.Function):
+    """Causal sliding-window + sink-token + GQA attention (flash_attention_gpt_oss.py:340)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, window_size, sink_size, is_causal=True, softmax_scale=None):
+        _validate(q, k, v, is_causal)
+        if softmax_scale is None:
+            softmax_scale = 1.0 / math.sqrt(q.shape[-1])
+        o, lse = swa_forward(q, k, v, window_size, sink_size, softmax_scale)
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.softmax_scale = softmax_scale
+        ctx.window_size = window_size
+        ctx.sink_size = sink_size
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse = ctx.saved_tensors
+        dq, dk, dv = swa_backward(q, k, v, o, lse, do, ctx.window_size, ctx.sink_size,
+                                  ctx.softmax_scale)
+        return dq, dk, dv, None, None, None, None
+
+
+def flash_swda_with_sink(q, k, v, window_size: int, sink_size: int = 0, is_causal: bool = True,
+                         scale: Optional[float] = None):
+    """Same signature as the reference (flash_attention_gpt_oss.py:437-438)."""
+    return FlashSWDAWithSink.apply(q, k, v, window_size, sink_size, is_causal, scale)

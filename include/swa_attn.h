@@ -1,0 +1,130 @@
+/*
+ * swa_attn.h -- C ABI of the B200 (sm_100a) causal sliding-window + sink-token + GQA
+ * attention, forward and backward.
+ *
+ * This is the drop-in boundary for the reference project's autograd Function
+ * (junhown3/FlashAttention-GPT-OSS-finetuning, flash_attention_gpt_oss.py):
+ *
+ *   swa_fwd            replaces FlashSWDAWithSink.forward's kernel launch
+ *                      (flash_attention_gpt_oss.py:356-379: allocate o, M; launch
+ *                      _flash_attention_forward_swa_kernel).
+ *   swa_bwd            replaces FlashSWDAWithSink.backward's work
+ *                      (flash_attention_gpt_oss.py:397-435: Delta in torch, launch
+ *                      _flash_attention_backward_swa_kernel, cast dk/dv).
+ *   swa_bwd_preprocess the Delta = rowsum(dO * O) line (flash_attention_gpt_oss.py:403).
+ *   swa_bwd_dq         the dQ half of _flash_attention_backward_swa_kernel
+ *                      (flash_attention_gpt_oss.py:316-321, 334-338).
+ *   swa_bwd_dkdv       the dK/dV half of that kernel (flash_attention_gpt_oss.py:295-304,
+ *                      323-332), made deterministic: no atomics.
+ *
+ * Conventions
+ *   - Tensors are [B, H, L, D] with the last dimension contiguous; the strides of the first
+ *     three dimensions are given in ELEMENTS (like the reference's x.stride(0..2)).
+ *   - q, o, dout, dq: [B, Hq, L, D]; k, v, dk, dv: [B, Hkv, L, D]; one dtype for all of
+ *     them (fp16 or bf16).  Query head h reads KV head h / (Hq / Hkv).
+ *   - Key j is visible to query i iff j <= i and (i - j < window_size or j < sink_size).
+ *   - lse: [B, Hq, L] fp32, contiguous.  It is private to this library: it holds the
+ *     base-2 log-sum-exp of the scaled scores (log2(e) * ln-LSE), -inf for a row that sees
+ *     no key.  (The reference saves the row maximum M instead.)
+ *   - Every entry point is asynchronous on `stream` (a cudaStream_t, NULL = legacy default
+ *     stream), allocates nothing, and returns a SwaStatus.  Work on the device never
+ *     waits on another launch.
+ */
+#ifndef SWA_ATTN_H_
+#define SWA_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SWA_API __attribute__((visibility("default")))
+#else
+#define SWA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum SwaStatus {
+  SWA_OK = 0,
+  SWA_ERR_INVALID_ARG = 1,   /* null pointer, negative size, inconsistent shapes        */
+  SWA_ERR_UNSUPPORTED = 2,   /* head_dim / dtype / alignment this build does not cover  */
+  SWA_ERR_LAUNCH = 3,        /* the CUDA launch itself failed (see swa_last_cuda_error) */
+  SWA_ERR_DEVICE_TIMEOUT = 4,/* a bounded on-device wait gave up                        */
+  SWA_ERR_WORKSPACE = 5      /* workspace missing or smaller than swa_bwd_workspace_size */
+} SwaStatus;
+
+typedef enum SwaDtype { SWA_F16 = 0, SWA_BF16 = 1 } SwaDtype;
+
+/* Problem description shared by all entry points. */
+typedef struct SwaProblem {
+  int32_t batch;        /* B   */
+  int32_t n_q_heads;    /* Hq  */
+  int32_t n_kv_heads;   /* Hkv (Hq % Hkv == 0) */
+  int32_t seq_len;      /* L   */
+  int32_t head_dim;     /* D: 16, 32, 64 or 128 in this build (reference allows D <= 128) */
+  int32_t window_size;  /* W: counts the diagonal; W <= 0 leaves only the sinks visible   */
+  int32_t sink_size;    /* S: first S key positions always visible (causally)            */
+  int32_t dtype;        /* SwaDtype */
+  float softmax_scale;  /* scale applied to QK^T (the reference defaults it to 1/sqrt(D)) */
+} SwaProblem;
+
+/* A [B, H, L, D] tensor: device pointer + element strides of dims 0..2 (dim 3 stride 1). */
+typedef struct SwaTensor {
+  void* ptr;
+  int64_t stride_b, stride_h, stride_l;
+} SwaTensor;
+
+typedef struct SwaFwdArgs {
+  SwaProblem p;
+  SwaTensor q, k, v;  /* inputs  */
+  SwaTensor o;        /* output, [B, Hq, L, D] */
+  float* lse;         /* output, [B, Hq, L] contiguous fp32 */
+} SwaFwdArgs;
+
+typedef struct SwaBwdArgs {
+  SwaProblem p;
+  SwaTensor q, k, v, o, dout;  /* inputs (o and lse from swa_fwd) */
+  const float* lse;
+  SwaTensor dq, dk, dv;        /* outputs, dtype of the inputs */
+  void* workspace;             /* device scratch, >= swa_bwd_workspace_size(&p) bytes, 256-B aligned */
+  size_t workspace_bytes;
+} SwaBwdArgs;
+
+/* Forward: o = softmax(mask(scale * q k^T)) v and the row log-sum-exp.
+ * Replaces flash_attention_gpt_oss.py:356-379. */
+SWA_API int swa_fwd(const SwaFwdArgs* args, void* stream);
+
+/* Scratch the backward needs (Delta rows and the sink-key partial sums), in bytes. */
+SWA_API size_t swa_bwd_workspace_size(const SwaProblem* p);
+
+/* Full backward: preprocess + dK/dV + dQ.  Replaces flash_attention_gpt_oss.py:397-435. */
+SWA_API int swa_bwd(const SwaBwdArgs* args, void* stream);
+
+/* Delta[b,h,i] = sum_d dout * o, written to the front of the workspace.
+ * Replaces flash_attention_gpt_oss.py:403. */
+SWA_API int swa_bwd_preprocess(const SwaBwdArgs* args, void* stream);
+
+/* dq; needs swa_bwd_preprocess to have run on the same workspace.
+ * Replaces flash_attention_gpt_oss.py:306-321, 334-338. */
+SWA_API int swa_bwd_dq(const SwaBwdArgs* args, void* stream);
+
+/* dk, dv, deterministic (each KV tile owned by one CTA, GQA group looped inside);
+ * needs swa_bwd_preprocess.  Replaces flash_attention_gpt_oss.py:295-304, 323-332. */
+SWA_API int swa_bwd_dkdv(const SwaBwdArgs* args, void* stream);
+
+/* Human-readable name of a SwaStatus. */
+SWA_API const char* swa_status_string(int status);
+
+/* Text of the last CUDA error seen by a launch on this host thread ("" if none). */
+SWA_API const char* swa_last_cuda_error(void);
+
+/* Version of this library (major*10000 + minor*100 + patch). */
+SWA_API int swa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SWA_ATTN_H_ */

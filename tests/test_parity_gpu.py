@@ -1,0 +1,171 @@
+"""GPU parity: the CUDA kernels (through the drop-in autograd Function, i.e. the C-ABI
+library) against the CPU oracle on the same seeded, dtype-rounded inputs.
+
+Bar (tolerance of the task statement): max|x - ref| / max|ref| <= 2e-3 for fp16 and
+<= 1.5e-2 for bf16, for O, dQ, dK and dV, the oracle computing in fp64.
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import swa_oracle as orc
+from tests._pkg import pkg, submodule
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float16: 2e-3, torch.bfloat16: 1.5e-2}
+GOLDEN = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "golden_*.npz")))
+
+
+def _rel(x, ref):
+    x = x.detach().double().cpu()
+    ref = ref.detach().double().cpu()
+    den = ref.abs().max().item()
+    if den == 0:
+        return x.abs().max().item()
+    return (x - ref).abs().max().item() / den
+
+
+def run_ours(q, k, v, do, w, s, scale=None):
+    dev = torch.device("cuda:0")
+    q, k, v = (t.to(dev).detach().requires_grad_() for t in (q, k, v))
+    o = pkg().flash_swda_with_sink(q, k, v, w, s, True, scale)
+    o.backward(do.to(dev))
+    torch.cuda.synchronize()
+    return o.detach(), q.grad, k.grad, v.grad
+
+
+def check(q, k, v, do, w, s, scale=None, tol=None, chunked=False):
+    tol = tol or TOL[q.dtype]
+    ours = run_ours(q, k, v, do, w, s, scale)
+    if chunked:
+        ref = orc.backward_chunked(q.float(), k.float(), v.float(), do.float(), w, s, scale,
+                                   compute_dtype=torch.float64)
+    else:
+        ref = orc.backward(q.float(), k.float(), v.float(), do.float(), w, s, scale)
+    errs = {n: _rel(a, b) for n, a, b in zip(("o", "dq", "dk", "dv"), ours, ref)}
+    for n, a in zip(("o", "dq", "dk", "dv"), ours):
+        assert torch.isfinite(a).all(), f"{n} has non-finite values"
+    bad = {n: e for n, e in errs.items() if not e <= tol}
+    assert not bad, f"tolerance {tol} exceeded: {errs}"
+    return errs
+
+
+def rand(shape_q, shape_k, dtype, seed, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(shape_q, generator=g) * scale
+    k = torch.randn(shape_k, generator=g) * scale
+    v = torch.randn(shape_k, generator=g) * scale
+    do = torch.randn(shape_q, generator=g) * scale
+    return tuple(t.to(dtype) for t in (q, k, v, do))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+@pytest.mark.parametrize("path", GOLDEN, ids=[os.path.basename(f)[7:-4] for f in GOLDEN])
+def test_golden_cases(path, dtype):
+    z = np.load(path)
+    b, hq, hkv, l, d, w, s, _ = (int(x) for x in z["shape"])
+    q, k, v, do = (torch.from_numpy(z[n]).to(dtype) for n in ("q", "k", "v", "do"))
+    check(q, k, v, do, w, s)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+@pytest.mark.parametrize("L", [1, 2, 63, 64, 65, 127, 128, 129, 255, 300])
+def test_ragged_lengths(L, dtype):
+    q, k, v, do = rand((2, 4, L, 64), (2, 2, L, 64), dtype, L)
+    check(q, k, v, do, 37, 3)
+
+
+@pytest.mark.parametrize("d", [16, 32, 64, 128])
+@pytest.mark.parametrize("w,s", [(1, 0), (1, 5), (0, 3), (64, 4), (130, 70), (10**9, 0),
+                                 (200, 200), (5, 1000)])
+def test_window_sink_grid(d, w, s):
+    q, k, v, do = rand((1, 4, 211, d), (1, 1, 211, d), torch.float16, d * 1000 + w % 997 + s)
+    check(q, k, v, do, w, s)
+
+
+def test_no_visible_keys_gives_zero():
+    q, k, v, do = rand((1, 2, 70, 32), (1, 2, 70, 32), torch.bfloat16, 9)
+    o, dq, dk, dv = run_ours(q, k, v, do, 0, 0)
+    for t in (o, dq, dk, dv):
+        assert (t == 0).all()
+
+
+@pytest.mark.parametrize("hq,hkv", [(16, 1), (8, 8), (12, 3)])
+def test_gqa_groups(hq, hkv):
+    q, k, v, do = rand((2, hq, 160, 64), (2, hkv, 160, 64), torch.bfloat16, hq * 10 + hkv)
+    check(q, k, v, do, 48, 4)
+
+
+@pytest.mark.parametrize("d", [8, 48, 80, 96, 112])
+def test_head_dims_padded(d):
+    q, k, v, do = rand((1, 4, 150, d), (1, 2, 150, d), torch.float16, d)
+    check(q, k, v, do, 40, 4)
+
+
+def test_custom_scale():
+    q, k, v, do = rand((1, 4, 130, 64), (1, 2, 130, 64), torch.float16, 11)
+    check(q, k, v, do, 50, 2, scale=0.3)
+
+
+def test_non_contiguous_layouts():
+    # [B, L, H, D] storage viewed as [B, H, L, D] (strided heads), as from a fused QKV projection
+    g = torch.Generator().manual_seed(5)
+    base_q = torch.randn(2, 190, 8, 64, generator=g).to(torch.bfloat16)
+    base_k = torch.randn(2, 190, 2, 64, generator=g).to(torch.bfloat16)
+    base_v = torch.randn(2, 190, 2, 64, generator=g).to(torch.bfloat16)
+    do = torch.randn(2, 8, 190, 64, generator=g).to(torch.bfloat16)
+    q, k, v = (t.transpose(1, 2) for t in (base_q, base_k, base_v))
+    dev = torch.device("cuda:0")
+    qd, kd, vd = (t.to(dev).transpose(1, 2).contiguous().transpose(1, 2) for t in (q, k, v))
+    assert not qd.is_contiguous()
+    qd, kd, vd = (t.detach().requires_grad_() for t in (qd, kd, vd))
+    o = pkg().flash_swda_with_sink(qd, kd, vd, 33, 4)
+    o.backward(do.to(dev))
+    ref = orc.backward(q.float(), k.float(), v.float(), do.float(), 33, 4)
+    for a, r in zip((o, qd.grad, kd.grad, vd.grad), ref):
+        assert _rel(a, r) <= TOL[torch.bfloat16]
+
+
+def test_backward_is_deterministic():
+    q, k, v, do = rand((2, 8, 700, 64), (2, 2, 700, 64), torch.bfloat16, 21)
+    r1 = run_ours(q, k, v, do, 100, 4)
+    r2 = run_ours(q, k, v, do, 100, 4)
+    for a, b in zip(r1, r2):
+        assert torch.equal(a, b)
+
+
+def test_forward_lse_matches_oracle():
+    f = submodule("flash_attention_gpt_oss")
+    q, k, v, _ = rand((1, 4, 300, 64), (1, 2, 300, 64), torch.float16, 3)
+    dev = torch.device("cuda:0")
+    o, lse2 = f.swa_forward(q.to(dev), k.to(dev), v.to(dev), 77, 5)
+    ref_o, ref_lse = orc.forward(q.float(), k.float(), v.float(), 77, 5)
+    assert _rel(o, ref_o) <= 2e-3
+    lse_nat = lse2.double().cpu() / orc.LOG2E
+    assert (lse_nat - ref_lse).abs().max().item() < 1e-3
+
+
+@pytest.mark.parametrize("name", ["cfg1_ref_bench"])
+def test_baseline_config_full(name):
+    wl = submodule("workloads")
+    w = wl.CONFIGS[name]
+    q, k, v, do = wl.make_inputs(w)
+    check(q, k, v, do, w.window_size, w.sink_size, chunked=True)
+
+
+@pytest.mark.parametrize("name,kw", [
+    ("cfg2_gptoss_swa", dict(batch=1, n_q_heads=16, n_kv_heads=2, seq_len=1024)),
+    ("cfg3_full_causal", dict(batch=1, n_q_heads=8, n_kv_heads=1, seq_len=1024, window_size=1024)),
+    ("cfg4_long_swa", dict(n_q_heads=8, n_kv_heads=1, seq_len=4096)),
+    ("cfg5_ragged_s0", dict(batch=1, n_q_heads=8, n_kv_heads=1)),
+    ("cfg5_ragged_s16", dict(batch=1, n_q_heads=8, n_kv_heads=1)),
+])
+def test_baseline_configs_reduced(name, kw):
+    wl = submodule("workloads")
+    w = wl.CONFIGS[name].replace(**kw)
+    q, k, v, do = wl.make_inputs(w)
+    check(q, k, v, do, w.window_size, w.sink_size, chunked=True)
