@@ -18,6 +18,8 @@ SWA_ERR_UNSUPPORTED = 2
 SWA_ERR_LAUNCH = 3
 SWA_ERR_DEVICE_TIMEOUT = 4
 SWA_ERR_WORKSPACE = 5
+SWA_ERR_TOO_LARGE = 6
+SWA_NO_ALLOC_SCRATCH_BYTES = 16 << 20
 
 SWA_F16 = 0
 SWA_BF16 = 1
@@ -25,7 +27,7 @@ SWA_BF16 = 1
 # Every extern "C" symbol include/swa_attn.h declares.
 EXPORTED_SYMBOLS = (
     "swa_fwd", "swa_bwd", "swa_bwd_preprocess", "swa_bwd_dq", "swa_bwd_dkdv",
-    "swa_bwd_workspace_size", "swa_status_string", "swa_last_cuda_error", "swa_version",
+    "swa_bwd_workspace_size", "swa_bwd_no_alloc", "swa_status_string", "swa_last_cuda_error", "swa_version",
 )
 
 
@@ -74,6 +76,7 @@ STATUS_NAMES = {
     SWA_ERR_UNSUPPORTED: "unsupported shape, dtype or layout", SWA_ERR_LAUNCH: "CUDA launch failed",
     SWA_ERR_DEVICE_TIMEOUT: "on-device wait timed out",
     SWA_ERR_WORKSPACE: "workspace missing, misaligned or too small",
+    SWA_ERR_TOO_LARGE: "problem needs more scratch than the static no-alloc workspace",
 }
 
 _lib = None
@@ -83,7 +86,7 @@ _lock = threading.Lock()
 def _declare(l):
     P = ctypes.POINTER
     l.swa_fwd.argtypes = [P(SwaFwdArgs), ctypes.c_void_p]
-    for name in ("swa_bwd", "swa_bwd_preprocess", "swa_bwd_dq", "swa_bwd_dkdv"):
+    for name in ("swa_bwd", "swa_bwd_preprocess", "swa_bwd_dq", "swa_bwd_dkdv", "swa_bwd_no_alloc"):
         getattr(l, name).argtypes = [P(SwaBwdArgs), ctypes.c_void_p]
         getattr(l, name).restype = ctypes.c_int
     l.swa_fwd.restype = ctypes.c_int

@@ -3,6 +3,7 @@
 // requirements of these kernels), dtype/head-dim dispatch and error reporting.
 #include <string.h>
 
+#include <mutex>
 #include <string>
 
 #include "swa_common.cuh"
@@ -133,6 +134,7 @@ const char* swa_status_string(int s) {
     case SWA_ERR_LAUNCH: return "CUDA launch failed";
     case SWA_ERR_DEVICE_TIMEOUT: return "on-device wait timed out";
     case SWA_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+    case SWA_ERR_TOO_LARGE: return "problem needs more scratch than the static no-alloc workspace";
     default: return "unknown status";
   }
 }
@@ -195,3 +197,48 @@ int swa_bwd(const SwaBwdArgs* a, void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// swa_bwd_no_alloc: the backward with its scratch in a static device array.
+// ---------------------------------------------------------------------------------------
+namespace {
+
+// The scratch of swa_bwd_no_alloc.  In host code this name is only a host-side stand-in: a
+// kernel must be given the device address that cudaGetSymbolAddress returns.
+static __device__ __align__(256) unsigned char g_no_alloc_scratch[SWA_NO_ALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_no_alloc_mu;
+void* g_no_alloc_ptr[kMaxDevices] = {};
+
+// Device address of g_no_alloc_scratch on the current device, looked up once per device.
+int no_alloc_scratch(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return record(e);
+  if (dev < 0 || dev >= kMaxDevices) return SWA_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_no_alloc_mu);
+  if (!g_no_alloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_no_alloc_scratch);
+    if (e != cudaSuccess) return record(e);
+    g_no_alloc_ptr[dev] = p;
+  }
+  *out = g_no_alloc_ptr[dev];
+  return SWA_OK;
+}
+
+}  // namespace
+
+extern "C" int swa_bwd_no_alloc(const SwaBwdArgs* a, void* stream) {
+  if (!a) return SWA_ERR_INVALID_ARG;
+  int st = check_problem(a->p);
+  if (st) return st;
+  if (swa_bwd_workspace_size(&a->p) > SWA_NO_ALLOC_SCRATCH_BYTES) return SWA_ERR_TOO_LARGE;
+  void* scratch = nullptr;
+  if ((st = no_alloc_scratch(&scratch))) return st;
+  SwaBwdArgs b = *a;
+  b.workspace = scratch;
+  b.workspace_bytes = SWA_NO_ALLOC_SCRATCH_BYTES;
+  return swa_bwd(&b, stream);
+}

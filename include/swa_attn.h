@@ -52,7 +52,8 @@ typedef enum SwaStatus {
   SWA_ERR_UNSUPPORTED = 2,   /* head_dim / dtype / alignment this build does not cover  */
   SWA_ERR_LAUNCH = 3,        /* the CUDA launch itself failed (see swa_last_cuda_error) */
   SWA_ERR_DEVICE_TIMEOUT = 4,/* a bounded on-device wait gave up                        */
-  SWA_ERR_WORKSPACE = 5      /* workspace missing or smaller than swa_bwd_workspace_size */
+  SWA_ERR_WORKSPACE = 5,     /* workspace missing or smaller than swa_bwd_workspace_size */
+  SWA_ERR_TOO_LARGE = 6      /* problem needs more scratch than swa_bwd_no_alloc holds   */
 } SwaStatus;
 
 typedef enum SwaDtype { SWA_F16 = 0, SWA_BF16 = 1 } SwaDtype;
@@ -113,6 +114,22 @@ SWA_API int swa_bwd_dq(const SwaBwdArgs* args, void* stream);
 /* dk, dv, deterministic (each KV tile owned by one CTA, GQA group looped inside);
  * needs swa_bwd_preprocess.  Replaces flash_attention_gpt_oss.py:295-304, 323-332. */
 SWA_API int swa_bwd_dkdv(const SwaBwdArgs* args, void* stream);
+
+/* Backward that allocates nothing and takes no workspace.  No counterpart in the reference.
+ *
+ * For callers that cannot call cudaMalloc: a host that hands this library only its tensors
+ * (an FFI/ctypes binding with no device allocator of its own, an engine that owns all device
+ * memory through a fixed pool and forbids side allocations).  Same inputs, outputs and
+ * results as swa_bwd; args->workspace and args->workspace_bytes are ignored.  Its scratch is
+ * a static device array of SWA_NO_ALLOC_SCRATCH_BYTES (16 MiB) that every GPU which loads
+ * this library keeps until the process exits; problems whose swa_bwd_workspace_size exceeds
+ * it get SWA_ERR_TOO_LARGE.  The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current, so make that first call before
+ * any stream capture.  All calls share the one array and each call writes every scratch byte
+ * it reads, so nothing carries over between calls, but calls that overlap on the GPU (other
+ * streams, other host threads, same device) race on it: serialise them. */
+#define SWA_NO_ALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+SWA_API int swa_bwd_no_alloc(const SwaBwdArgs* args, void* stream);
 
 /* Human-readable name of a SwaStatus. */
 SWA_API const char* swa_status_string(int status);

@@ -120,3 +120,14 @@ def test_python_validation_matches_reference_asserts():
 def test_kernel_head_dim_padding_rule():
     f = submodule("flash_attention_gpt_oss")
     assert [f._kernel_head_dim(d) for d in (1, 16, 17, 48, 64, 80, 128)] == [16, 16, 32, 64, 64, 128, 128]
+
+
+def test_no_alloc_rejects_problems_beyond_its_static_scratch():
+    L = submodule("_lib")
+    lib = pkg().lib()
+    big = _problem(n_q_heads=64, n_kv_heads=8, seq_len=131072)   # 32 MiB of Delta rows
+    assert lib.swa_bwd_workspace_size(ctypes.byref(big)) > L.SWA_NO_ALLOC_SCRATCH_BYTES
+    t = L.SwaTensor(1 << 20, 1 << 20, 1 << 14, 64)
+    args = L.SwaBwdArgs(big, t, t, t, t, t, 1 << 20, t, t, t, None, 0)
+    assert lib.swa_bwd_no_alloc(ctypes.byref(args), None) == L.SWA_ERR_TOO_LARGE
+    assert lib.swa_bwd_no_alloc(None, None) == L.SWA_ERR_INVALID_ARG
