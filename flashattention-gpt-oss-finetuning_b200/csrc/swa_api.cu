@@ -10,7 +10,7 @@
 #include "swa_params.cuh"
 
 namespace swa {
-template <typename T, int D> cudaError_t launch_fwd_mma(const FwdParams&, cudaStream_t);
+template <typename T, int D> cudaError_t launch_fwd_tc(const FwdParams&, cudaStream_t, int*);
 template <typename T, int D> cudaError_t launch_bwd_preprocess(const BwdParams&, cudaStream_t);
 template <typename T, int D> cudaError_t launch_bwd_dq_mma(const BwdParams&, cudaStream_t);
 template <typename T, int D> cudaError_t launch_bwd_dkdv_mma(const BwdParams&, cudaStream_t);
@@ -19,6 +19,26 @@ template <typename T, int D> cudaError_t launch_bwd_dkdv_mma(const BwdParams&, c
 namespace {
 
 thread_local std::string g_last_cuda_error;
+
+// Set by a kernel when one of its bounded on-device waits gives up (each device has its own
+// copy).  Host code passes the device address obtained from cudaGetSymbolAddress.
+static __device__ int g_device_error;
+
+constexpr int kMaxDev = 64;
+std::mutex g_err_mu;
+int* g_err_ptr[kMaxDev] = {};
+
+int* device_error_ptr() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return nullptr;
+  std::lock_guard<std::mutex> lock(g_err_mu);
+  if (!g_err_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    g_err_ptr[dev] = static_cast<int*>(p);
+  }
+  return g_err_ptr[dev];
+}
 
 int record(cudaError_t e) {
   if (e == cudaSuccess) return SWA_OK;
@@ -77,7 +97,9 @@ int dispatch(const SwaProblem& pr, const P& kp, cudaStream_t st) {
 }
 
 template <typename T, int D> struct Fwd {
-  static cudaError_t run(const swa::FwdParams& p, cudaStream_t s) { return swa::launch_fwd_mma<T, D>(p, s); }
+  static cudaError_t run(const swa::FwdParams& p, cudaStream_t s) {
+    return swa::launch_fwd_tc<T, D>(p, s, device_error_ptr());
+  }
 };
 template <typename T, int D> struct Pre {
   static cudaError_t run(const swa::BwdParams& p, cudaStream_t s) { return swa::launch_bwd_preprocess<T, D>(p, s); }
@@ -140,6 +162,19 @@ const char* swa_status_string(int s) {
 }
 
 const char* swa_last_cuda_error(void) { return g_last_cuda_error.c_str(); }
+
+int swa_check_device(void* stream) {
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return record(e);
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int));
+  if (e != cudaSuccess) return record(e);
+  if (v == 0) return SWA_OK;
+  const int zero = 0;
+  e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+  if (e != cudaSuccess) return record(e);
+  return SWA_ERR_DEVICE_TIMEOUT;
+}
 
 size_t swa_bwd_workspace_size(const SwaProblem* p) {
   if (!p) return 0;

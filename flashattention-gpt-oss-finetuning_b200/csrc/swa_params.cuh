@@ -17,6 +17,7 @@ struct FwdParams {
   Strides sq, sk, sv, so;
   int B, Hq, Hkv, L, W, S;
   float scale_log2;  // softmax_scale * log2(e)
+  int sink_box;      // keys per sink segment (tensor-core forward)
 };
 
 struct BwdParams {

@@ -34,8 +34,14 @@ def run_ours(q, k, v, do, w, s, scale=None):
     q, k, v = (t.to(dev).detach().requires_grad_() for t in (q, k, v))
     o = pkg().flash_swda_with_sink(q, k, v, w, s, True, scale)
     o.backward(do.to(dev))
-    torch.cuda.synchronize()
+    assert_device_ok(dev)
     return o.detach(), q.grad, k.grad, v.grad
+
+
+def assert_device_ok(dev):
+    L = submodule("_lib")
+    st = L.lib().swa_check_device(torch.cuda.current_stream(dev).cuda_stream)
+    assert st == L.SWA_OK, f"device status {st}: {L.STATUS_NAMES.get(st)}"
 
 
 def check(q, k, v, do, w, s, scale=None, tol=None, chunked=False):
