@@ -178,4 +178,28 @@ __device__ __forceinline__ void load_tile_async(T* smem, const T* gbase, int64_t
   }
 }
 
+// Number of CTAs for a persistent kernel: resident CTAs per SM (limited by registers,
+// shared memory and the kernel's TMEM columns, 512 per SM) x SMs, at most `work`.
+template <typename K>
+inline int persistent_grid(K kern, int threads, int smem, int tmem_cols, int work) {
+  int dev = 0, sms = 0, smem_sm = 0, regs_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+  if (cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess)
+    return -1;
+  if (cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev) != cudaSuccess)
+    return -1;
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return -1;
+  int per_sm = tmem_cols > 0 ? 512 / tmem_cols : 32;
+  const int by_smem = smem_sm / (smem + (int)fa.sharedSizeBytes + 1024);
+  const int regs_cta = ((fa.numRegs * 32 + 255) / 256) * 256 * (threads / 32);
+  const int by_regs = regs_cta > 0 ? regs_sm / regs_cta : 32;
+  per_sm = per_sm < by_smem ? per_sm : by_smem;
+  per_sm = per_sm < by_regs ? per_sm : by_regs;
+  if (per_sm < 1) per_sm = 1;
+  const long long g = (long long)sms * per_sm;
+  return (int)(g < work ? g : (work > 0 ? work : 1));
+}
+
 }  // namespace swa
