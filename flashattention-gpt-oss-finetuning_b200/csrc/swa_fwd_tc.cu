@@ -1,24 +1,26 @@
 // swa_fwd_tc.cu -- forward kernel on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
 //
-// One CTA = one 128-row query tile of one (batch, query head).  It touches only the key
-// segments that hold sinks or fall inside the sliding window: sink segments of SB keys
-// (SB = S rounded up to 16, at most 128) below the window, then 128-key window tiles.
+// Persistent kernel: each CTA streams 128-row query tiles ("items") of (batch, query head);
+// for each item it touches only the key segments that hold sinks or fall inside the sliding
+// window: sink segments of SB keys (SB = S rounded up to 16, at most 64) below the window,
+// then 64-key window tiles.
 //
 // Warp roles (6 warps, 192 threads):
-//   warp 0   TMA producer: Q tile once, then K/V segments into a 2-stage shared-memory ring
-//            (128-byte / 64-byte / 32-byte swizzled, the UMMA canonical K-major layout).
-//   warp 1   MMA issuer (one thread): S = Q K^T into TMEM (M=128, N=segment width,
-//            K-major A and B from shared memory), then O += P V with P read from TMEM
-//            (A operand in TMEM) and V as an MN-major B operand.
-//   warps 2-5  softmax: thread t owns query row t (TMEM lane t).  Reads its S row with
-//            tcgen05.ld, masks, updates the running max, writes P (16-bit) to TMEM with
-//            tcgen05.st.  O is rescaled in TMEM only when the row max grows by more than
+//   warp 0   TMA producer: Q tiles (double-buffered) and K/V segments into a shared-memory
+//            ring, 128/64/32-byte swizzled (the UMMA canonical layouts); runs ahead across
+//            items.
+//   warp 1   MMA issuer (one thread): S_g = Q K_g^T into TMEM buffer g&1 one segment ahead of
+//            the softmax, then O += P_g V_g with P read from TMEM (A operand in TMEM) and V as
+//            an MN-major B operand.
+//   warps 2-5  softmax: thread t owns query row t (TMEM lane t).  Per 32-row warp block a
+//            segment that the block cannot see is skipped (P = 0) and one it sees completely
+//            is not masked.  O is rescaled in TMEM only when the row max grows by more than
 //            2^8 (the exponent base stays fixed otherwise, so P <= 256 and fp32 O and l stay
 //            exact up to that common factor).  Epilogue: O / l and the base-2 LSE.
 //
-// TMEM columns: S [0,128), P [128,192) (two 16-bit values per column), O [192, 192 + D).
-// Every mbarrier wait is bounded (sm100::mbar_wait); a wait that gives up records an error
-// in `err` and the CTA leaves its loops, releases its TMEM and exits.
+// TMEM columns: S0 [0,64), S1 [64,128), P0 [128,160), P1 [160,192) (two 16-bit values per
+// column), O [192, 192 + D).  Every mbarrier wait is bounded (sm100::mbar_wait); a wait that
+// gives up records an error in `err` and the CTA leaves its loops, frees TMEM and exits.
 //
 // Reference behaviour followed: _flash_attention_forward_swa_kernel
 // (flash_attention_gpt_oss.py:7-180): visibility rule, online softmax in base 2, O = 0 for a
@@ -39,7 +41,7 @@ struct FwdTmaps {
 
 template <int D>
 struct FwdCfg {
-  static constexpr int BM = 128, BN = 128, NST = 2;
+  static constexpr int BM = 128, BN = 64, NST = 3;
   static constexpr int CW = D < 64 ? D : 64;  // elements per swizzled smem row
   static constexpr int NCH = D / CW;          // chunks along the head dim
   static constexpr int ROWB = CW * 2;         // bytes per smem row
@@ -59,8 +61,8 @@ struct FwdSched {
       *key0 = t * sb;
       *rows = sb;
     } else {
-      *key0 = (win_lo + t - n_sink) * 128;
-      *rows = 128;
+      *key0 = (win_lo + t - n_sink) * 64;
+      *rows = 64;
     }
   }
 };
@@ -71,9 +73,9 @@ __device__ __forceinline__ FwdSched fwd_schedule(int q0, int L, int W, int S, in
   int sink_lim;
   if (W > 0) {
     const int lo = max(0, q0 - W + 1);
-    f.win_lo = lo / 128;
-    f.n_win = q_last / 128 - f.win_lo + 1;
-    sink_lim = f.win_lo * 128;
+    f.win_lo = lo / 64;
+    f.n_win = q_last / 64 - f.win_lo + 1;
+    sink_lim = f.win_lo * 64;
   } else {
     f.win_lo = 0;
     f.n_win = 0;
@@ -89,15 +91,24 @@ __device__ __forceinline__ void record_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// Work item = one 128-row query tile of one (batch, query head).  Items are numbered with the
+// query head fastest, so CTAs running at the same time read the same K/V rows (one GQA group)
+// and share them through L2.
+__device__ __forceinline__ void decode_item(int it, int Hq, int n_qt, int* b, int* h, int* qt) {
+  *h = it % Hq;
+  const int rest = it / Hq;
+  *qt = rest % n_qt;
+  *b = rest / n_qt;
+}
 
-// Mask one row segment of N scores in place (masked -> NEG) and return the scaled row max
-// (-inf if nothing is visible).  Visible columns c: c <= c_hi and (c >= c_lo or c < c_sk).
-// Masked entries hold NEG so that NEG * scale = -inf for either sign of the scale; the row
-// extreme of the raw scores (max for scale >= 0, min otherwise) gives the max of the scaled
-// ones.  Independent partial extremes keep the dependency chains short.
+// Mask N scores in place (masked -> NEG) and return the scaled row max (-inf if nothing is
+// visible).  Visible columns c: c <= c_hi and (c >= c_lo or c < c_sk).  Masked entries hold
+// NEG so that NEG * scale = -inf for either sign of the scale; the row extreme of the raw
+// scores (max for scale >= 0, min otherwise) gives the max of the scaled ones.  Independent
+// partial extremes keep the dependency chains short.
 template <int N>
-__device__ __forceinline__ float mask_and_extreme(float* s, bool full, int c_lo, int c_hi, int c_sk,
-                                                  bool pos, float NEG, float sl2) {
+__device__ __forceinline__ float mask_and_max(float* s, bool full, int c_lo, int c_hi, int c_sk,
+                                              bool pos, float NEG, float sl2) {
   if (!full) {
     if (c_sk <= 0) {
 #pragma unroll
@@ -107,44 +118,26 @@ __device__ __forceinline__ float mask_and_extreme(float* s, bool full, int c_lo,
       for (int c = 0; c < N; ++c) s[c] = (c <= c_hi && (c >= c_lo || c < c_sk)) ? s[c] : NEG;
     }
   }
-  float e[8];
+  constexpr int K = N < 8 ? N : 8;
+  float e[K];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) e[k] = NEG;
+  for (int k = 0; k < K; ++k) e[k] = s[k];
   if (pos) {
 #pragma unroll
-    for (int c = 0; c < N; ++c) e[c & 7] = fmaxf(e[c & 7], s[c]);
+    for (int c = K; c < N; ++c) e[c % K] = fmaxf(e[c % K], s[c]);
 #pragma unroll
-    for (int k = 4; k > 0; k >>= 1)
+    for (int k = K / 2; k > 0; k >>= 1)
 #pragma unroll
       for (int j = 0; j < k; ++j) e[j] = fmaxf(e[j], e[j + k]);
   } else {
 #pragma unroll
-    for (int c = 0; c < N; ++c) e[c & 7] = fminf(e[c & 7], s[c]);
+    for (int c = K; c < N; ++c) e[c % K] = fminf(e[c % K], s[c]);
 #pragma unroll
-    for (int k = 4; k > 0; k >>= 1)
+    for (int k = K / 2; k > 0; k >>= 1)
 #pragma unroll
       for (int j = 0; j < k; ++j) e[j] = fminf(e[j], e[j + k]);
   }
   return (e[0] == NEG) ? -INFINITY : e[0] * sl2;
-}
-
-// O *= alpha for the rows that need it (warp-uniform: tcgen05.ld/st are warp-collective).
-// O is stable when this runs: the commit behind the S barrier also covers the previous PV.
-template <int D>
-__device__ __forceinline__ void rescale_o(uint32_t tO_lane, bool rescale, float m_used, float m_new,
-                                          float* l) {
-  if (!__any_sync(0xffffffffu, rescale)) return;
-  const float alpha = rescale ? fast_exp2(m_used - m_new) : 1.f;
-#pragma unroll
-  for (int c0 = 0; c0 < D; c0 += 16) {
-    uint32_t o[16];
-    tmem_ld16(tO_lane + c0, o);
-    tmem_ld_wait();
-#pragma unroll
-    for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-    tmem_st16(tO_lane + c0, o);
-  }
-  *l *= alpha;
 }
 
 // P = 2^(s * scale - base) for N columns, packed to 16-bit pairs and stored to TMEM (N/2
@@ -167,14 +160,45 @@ __device__ __forceinline__ float exp_pack_store(const float* s, float sl2, float
   return (acc[0] + acc[1]) + (acc[2] + acc[3]);
 }
 
-// Work item = one 128-row query tile of one (batch, query head).  Items are numbered with the
-// query head fastest, so CTAs running at the same time read the same K/V rows (one GQA group)
-// and share them through L2.
-__device__ __forceinline__ void decode_item(int it, int Hq, int n_qt, int* b, int* h, int* qt) {
-  *h = it % Hq;
-  const int rest = it / Hq;
-  *qt = rest % n_qt;
-  *b = rest / n_qt;
+template <int N>
+__device__ __forceinline__ void load_s(uint32_t taddr, float* s) {
+  if constexpr (N == 64) {
+    tmem_ld32(taddr, reinterpret_cast<uint32_t*>(s));
+    tmem_ld32(taddr + 32, reinterpret_cast<uint32_t*>(s + 32));
+  } else if constexpr (N == 48) {
+    tmem_ld32(taddr, reinterpret_cast<uint32_t*>(s));
+    tmem_ld16(taddr + 32, reinterpret_cast<uint32_t*>(s + 32));
+  } else if constexpr (N == 32) {
+    tmem_ld32(taddr, reinterpret_cast<uint32_t*>(s));
+  } else {
+    tmem_ld16(taddr, reinterpret_cast<uint32_t*>(s));
+  }
+  tmem_ld_wait();
+}
+
+// Per-row softmax state carried across the segments of one item.
+struct RowState {
+  float m_used;  // exponent base (scaled, base 2); -inf until a key is seen
+  float l;       // running sum of P
+};
+
+// One segment of N keys for this thread's row: P to TMEM, running max / sum updated.  Sets
+// `rescale` / `alpha` when O must be multiplied by alpha before the next PV (the caller does it
+// warp-uniformly after waiting for the previous PV).
+template <typename T, int N>
+__device__ __forceinline__ void softmax_segment(uint32_t tS_lane, uint32_t tP_lane, bool full, int c_lo,
+                                                int c_hi, int c_sk, bool pos, float NEG, float sl2,
+                                                RowState* rs, bool* rescale, float* alpha) {
+  float s[N];
+  load_s<N>(tS_lane, s);
+  const float m_tile = mask_and_max<N>(s, full, c_lo, c_hi, c_sk, pos, NEG, sl2);
+  const float m_new = fmaxf(rs->m_used, m_tile);
+  const bool grow = m_new > rs->m_used + 8.f;  // false when both are -inf
+  *rescale = grow && (rs->m_used != -INFINITY);
+  *alpha = *rescale ? fast_exp2(rs->m_used - m_new) : 1.f;
+  if (grow) rs->m_used = m_new;
+  const float base = (rs->m_used == -INFINITY) ? 0.f : rs->m_used;
+  rs->l = rs->l * (*alpha) + exp_pack_store<T, N>(s, sl2, base, tP_lane);
 }
 
 template <typename T, int D>
@@ -185,12 +209,12 @@ __global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* Qs = smem;                     // [2][Q_BYTES]
+  unsigned char* Qs = smem;                    // [2][Q_BYTES]
   unsigned char* KVs = smem + 2 * C::Q_BYTES;  // stage s: K at s*2*KV_BYTES, V after it
 
   __shared__ uint64_t bar_q_full[2], bar_q_empty[2];
   __shared__ uint64_t bar_full[C::NST], bar_empty[C::NST];
-  __shared__ uint64_t bar_s, bar_p, bar_o_full, bar_o_free;
+  __shared__ uint64_t bar_s[2], bar_p[2], bar_pv, bar_o_full, bar_o_free;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
 
@@ -208,13 +232,14 @@ __global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bar_q_full[s], 1);
       mbar_init(&bar_q_empty[s], 1);
+      mbar_init(&bar_s[s], 1);
+      mbar_init(&bar_p[s], 128);
     }
     for (int s = 0; s < C::NST; ++s) {
       mbar_init(&bar_full[s], 1);
       mbar_init(&bar_empty[s], 1);
     }
-    mbar_init(&bar_s, 1);
-    mbar_init(&bar_p, 128);
+    mbar_init(&bar_pv, 1);
     mbar_init(&bar_o_full, 1);
     mbar_init(&bar_o_free, 128);
     fence_mbar_init();
@@ -227,7 +252,6 @@ __global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
-  const uint32_t tS = tmem + C::S_COL, tP = tmem + C::P_COL, tO = tmem + C::O_COL;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -275,50 +299,84 @@ __global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
+    // Flattened sequence of (item, segment) pairs; S of pair g+1 is issued before PV of g.
     if (lane == 0 && !dead) {
-      int qi = 0, tg = 0;
-      bool ok = true;
       constexpr uint32_t id_o = idesc_f16(128, D, kBf16, false, true);
-      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-        int b, h, qt;
-        decode_item(it, Hq, n_qt, &b, &h, &qt);
-        const FwdSched sc = fwd_schedule(qt * C::BM, L, W, S, p.sink_box);
-        const int n = sc.n();
-        if (n == 0) continue;
-        const int qb = qi & 1;
-        if (!(ok = mbar_wait(&bar_q_full[qb], (qi >> 1) & 1, &abort_sh))) break;
-        const unsigned char* Qb = Qs + qb * C::Q_BYTES;
-        for (int t = 0; t < n; ++t, ++tg) {
-          const int st = tg % C::NST;
-          if (!(ok = mbar_wait(&bar_full[st], (tg / C::NST) & 1, &abort_sh))) break;
-          tc_fence_after();
-          int key0, rows;
-          sc.seg(t, &key0, &rows);
-          const unsigned char* Kb = KVs + st * 2 * C::KV_BYTES;
-          const unsigned char* Vb = Kb + C::KV_BYTES;
-          const uint32_t id_s = idesc_f16(128, rows, kBf16, false, false);
-#pragma unroll
-          for (int ks = 0; ks < D / 16; ++ks) {
-            const int ch = (ks * 16) / C::CW, within = (ks * 16) % C::CW;
-            const uint64_t ad = sdesc(saddr(Qb + ch * C::BM * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
-            const uint64_t bd = sdesc(saddr(Kb + ch * rows * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
-            mma_ss(tS, ad, bd, id_s, ks > 0 ? 1u : 0u);
-          }
-          mma_commit(&bar_s);
-          if (t == n - 1) mma_commit(&bar_q_empty[qb]);   // last read of this Q buffer
-          if (!(ok = mbar_wait(&bar_p, tg & 1, &abort_sh))) break;
-          // the previous item's epilogue must have read O before PV overwrites it
-          if (t == 0 && qi > 0 && !(ok = mbar_wait(&bar_o_free, (qi - 1) & 1, &abort_sh))) break;
-          tc_fence_after();
-          for (int ks = 0; ks < rows / 16; ++ks) {
-            const uint64_t bd = sdesc(saddr(Vb + ks * 16 * C::ROWB), rows * C::ROWB, 8 * C::ROWB, C::SWZ);
-            mma_ts(tO, tP + ks * 8, bd, id_o, (t > 0 || ks > 0) ? 1u : 0u);
-          }
-          mma_commit(&bar_empty[st]);
+      bool ok = true;
+      int s_it = blockIdx.x, s_t = 0, s_qi = 0, s_n = 0, s_g = 0;  // S cursor
+      FwdSched s_sc;
+      int v_it = blockIdx.x, v_t = 0, v_qi = 0, v_n = 0, v_g = 0;  // PV cursor
+      FwdSched v_sc;
+      auto next_item = [&](int& it, FwdSched& sc, int& n) -> bool {
+        for (; it < n_items; it += gridDim.x) {
+          int b, h, qt;
+          decode_item(it, Hq, n_qt, &b, &h, &qt);
+          sc = fwd_schedule(qt * C::BM, L, W, S, p.sink_box);
+          n = sc.n();
+          if (n > 0) return true;
         }
-        if (!ok) break;
-        mma_commit(&bar_o_full);
-        ++qi;
+        return false;
+      };
+      bool s_more = next_item(s_it, s_sc, s_n);
+      bool v_more = next_item(v_it, v_sc, v_n);
+      auto issue_s = [&]() -> bool {
+        const int qb = s_qi & 1;
+        if (s_t == 0 && !mbar_wait(&bar_q_full[qb], (s_qi >> 1) & 1, &abort_sh)) return false;
+        const int st = s_g % C::NST;
+        if (!mbar_wait(&bar_full[st], (s_g / C::NST) & 1, &abort_sh)) return false;
+        tc_fence_after();
+        int key0, rows;
+        s_sc.seg(s_t, &key0, &rows);
+        const unsigned char* Qb = Qs + qb * C::Q_BYTES;
+        const unsigned char* Kb = KVs + st * 2 * C::KV_BYTES;
+        const uint32_t id_s = idesc_f16(128, rows, kBf16, false, false);
+        const uint32_t tS = tmem + C::S_COL + (s_g & 1) * 64;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const int ch = (ks * 16) / C::CW, within = (ks * 16) % C::CW;
+          const uint64_t ad = sdesc(saddr(Qb + ch * C::BM * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
+          const uint64_t bd = sdesc(saddr(Kb + ch * rows * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
+          mma_ss(tS, ad, bd, id_s, ks > 0 ? 1u : 0u);
+        }
+        mma_commit(&bar_s[s_g & 1]);
+        if (s_t == s_n - 1) mma_commit(&bar_q_empty[qb]);  // last read of this Q buffer
+        ++s_g;
+        if (++s_t == s_n) {
+          s_t = 0;
+          ++s_qi;
+          s_it += gridDim.x;
+          s_more = next_item(s_it, s_sc, s_n);
+        }
+        return true;
+      };
+      if (s_more) ok = issue_s();
+      while (ok && v_more) {
+        // S one segment ahead: its S buffer was released by the softmax of segment v_g - 1,
+        // whose P barrier was waited for in the previous iteration.
+        if (s_more && !(ok = issue_s())) break;
+        if (!(ok = mbar_wait(&bar_p[v_g & 1], (v_g >> 1) & 1, &abort_sh))) break;
+        // the previous item's epilogue must have read O before the first PV overwrites it
+        if (v_t == 0 && v_qi > 0 && !(ok = mbar_wait(&bar_o_free, (v_qi - 1) & 1, &abort_sh))) break;
+        tc_fence_after();
+        int key0, rows;
+        v_sc.seg(v_t, &key0, &rows);
+        const int st = v_g % C::NST;
+        const unsigned char* Vb = KVs + st * 2 * C::KV_BYTES + C::KV_BYTES;
+        const uint32_t tP = tmem + C::P_COL + (v_g & 1) * 32;
+        for (int ks = 0; ks < rows / 16; ++ks) {
+          const uint64_t bd = sdesc(saddr(Vb + ks * 16 * C::ROWB), rows * C::ROWB, 8 * C::ROWB, C::SWZ);
+          mma_ts(tmem + C::O_COL, tP + ks * 8, bd, id_o, (v_t > 0 || ks > 0) ? 1u : 0u);
+        }
+        mma_commit(&bar_empty[st]);
+        mma_commit(&bar_pv);
+        ++v_g;
+        if (++v_t == v_n) {
+          mma_commit(&bar_o_full);
+          v_t = 0;
+          ++v_qi;
+          v_it += gridDim.x;
+          v_more = next_item(v_it, v_sc, v_n);
+        }
       }
       if (!ok) {
         abort_sh = 1;
@@ -332,82 +390,74 @@ __global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float sl2 = p.scale_log2;
     const bool pos = sl2 >= 0.f;
-    // Masked entries hold NEG so that NEG * scale = -inf for either sign of the scale; the
-    // row extreme of the raw scores (max for scale >= 0, min otherwise) gives the max of the
-    // scaled ones.
     const float NEG = pos ? -INFINITY : INFINITY;
-    int qi = 0, tg = 0;
+    int qi = 0, g = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
       int b, h, qt;
       decode_item(it, Hq, n_qt, &b, &h, &qt);
       const int q0 = qt * C::BM;
       const int i = q0 + r;
+      const int r0w = q0 + quad * 32;  // this warp's 32 rows
       const FwdSched sc = fwd_schedule(q0, L, W, S, p.sink_box);
       const int n = (ok && !dead) ? sc.n() : 0;
-      float m_used = -INFINITY, l = 0.f;
-      for (int t = 0; t < n; ++t, ++tg) {
-        if (!(ok = mbar_wait(&bar_s, tg & 1, &abort_sh))) break;
+      RowState rs{-INFINITY, 0.f};
+      for (int t = 0; t < n; ++t, ++g) {
+        if (!(ok = mbar_wait(&bar_s[g & 1], (g >> 1) & 1, &abort_sh))) break;
         tc_fence_after();
         int key0, rows;
         sc.seg(t, &key0, &rows);
-        // visible iff j <= i and (i - j < W or j < S)
-        const bool full = block_all_visible(q0, q0 + 128, key0, key0 + rows, W, S, L);
-        const int c_hi = i - key0;          // j <= i
-        const int c_lo = i - W + 1 - key0;  // i - j < W
-        const int c_sk = S - key0;          // j < S
-        float m_tile;
-        if (rows == 128) {
-          float s[128];
-#pragma unroll
-          for (int g = 0; g < 4; ++g) tmem_ld32(tS + lane_off + g * 32, reinterpret_cast<uint32_t*>(s + g * 32));
-          tmem_ld_wait();
-          m_tile = mask_and_extreme<128>(s, full, c_lo, c_hi, c_sk, pos, NEG, sl2);
-          const float m_new = fmaxf(m_used, m_tile);
-          const bool grow = m_new > m_used + 8.f;  // false when both are -inf
-          rescale_o<D>(tO + lane_off, grow && (m_used != -INFINITY), m_used, m_new, &l);
-          if (grow) m_used = m_new;
-          const float base = (m_used == -INFINITY) ? 0.f : m_used;
-          l += exp_pack_store<T, 128>(s, sl2, base, tP + lane_off);
+        const uint32_t tS = tmem + C::S_COL + (g & 1) * 64 + lane_off;
+        const uint32_t tP = tmem + C::P_COL + (g & 1) * 32 + lane_off;
+        if (block_none_visible(r0w, r0w + 32, key0, key0 + rows, W, S, L)) {
+          // nothing visible to this warp's rows: P = 0
+          const uint32_t z[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+          for (int c = 0; c < rows / 2; c += 8) tmem_st8(tP + c, z);
         } else {
-          // narrow sink segment: 16 columns at a time, two passes over TMEM
-          float ext = NEG;
-          for (int g = 0; g < rows / 16; ++g) {
-            float s[16];
-            tmem_ld16(tS + lane_off + g * 16, reinterpret_cast<uint32_t*>(s));
-            tmem_ld_wait();
-            ext = pos ? fmaxf(ext, mask_and_extreme<16>(s, full, c_lo - g * 16, c_hi - g * 16, c_sk - g * 16, pos, NEG, 1.f))
-                      : fminf(ext, -mask_and_extreme<16>(s, full, c_lo - g * 16, c_hi - g * 16, c_sk - g * 16, pos, NEG, -1.f));
+          const bool full = block_all_visible(r0w, r0w + 32, key0, key0 + rows, W, S, L);
+          const int c_hi = i - key0;          // j <= i
+          const int c_lo = i - W + 1 - key0;  // i - j < W
+          const int c_sk = S - key0;          // j < S
+          bool rescale = false;
+          float alpha = 1.f;
+          switch (rows) {
+            case 64: softmax_segment<T, 64>(tS, tP, full, c_lo, c_hi, c_sk, pos, NEG, sl2, &rs, &rescale, &alpha); break;
+            case 48: softmax_segment<T, 48>(tS, tP, full, c_lo, c_hi, c_sk, pos, NEG, sl2, &rs, &rescale, &alpha); break;
+            case 32: softmax_segment<T, 32>(tS, tP, full, c_lo, c_hi, c_sk, pos, NEG, sl2, &rs, &rescale, &alpha); break;
+            default: softmax_segment<T, 16>(tS, tP, full, c_lo, c_hi, c_sk, pos, NEG, sl2, &rs, &rescale, &alpha); break;
           }
-          m_tile = (ext == NEG) ? -INFINITY : ext * sl2;
-          const float m_new = fmaxf(m_used, m_tile);
-          const bool grow = m_new > m_used + 8.f;
-          rescale_o<D>(tO + lane_off, grow && (m_used != -INFINITY), m_used, m_new, &l);
-          if (grow) m_used = m_new;
-          const float base = (m_used == -INFINITY) ? 0.f : m_used;
-          for (int g = 0; g < rows / 16; ++g) {
-            float s[16];
-            tmem_ld16(tS + lane_off + g * 16, reinterpret_cast<uint32_t*>(s));
-            tmem_ld_wait();
-            mask_and_extreme<16>(s, full, c_lo - g * 16, c_hi - g * 16, c_sk - g * 16, pos, NEG, 1.f);
-            l += exp_pack_store<T, 16>(s, sl2, base, tP + lane_off + g * 8);
+          if (__any_sync(0xffffffffu, rescale)) {
+            // O must hold every PV issued so far: wait for the PV of segment g - 1 (t > 0 here,
+            // since a first segment never rescales).
+            if (!(ok = mbar_wait(&bar_pv, (g - 1) & 1, &abort_sh))) break;
+            tc_fence_after();
+#pragma unroll
+            for (int c0 = 0; c0 < D; c0 += 16) {
+              uint32_t o[16];
+              tmem_ld16(tmem + C::O_COL + lane_off + c0, o);
+              tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+              tmem_st16(tmem + C::O_COL + lane_off + c0, o);
+            }
           }
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&bar_p);
+        mbar_arrive(&bar_p[g & 1]);
       }
       if (n > 0 && ok) ok = mbar_wait(&bar_o_full, qi & 1, &abort_sh);
       if (n > 0 && ok) tc_fence_after();
       // ---- epilogue: O / l, base-2 LSE (a row that sees no key gets O = 0, LSE = -inf)
       const bool have_o = n > 0 && ok;
+      const float l = rs.l;
       const float inv = l > 0.f ? 1.f / l : 0.f;
       T* orow = static_cast<T*>(p.o) + b * p.so.b + h * p.so.h + (int64_t)i * p.so.l;
 #pragma unroll
       for (int c0 = 0; c0 < D; c0 += 16) {
         uint32_t o[16];
         if (have_o) {
-          tmem_ld16(tO + lane_off + c0, o);
+          tmem_ld16(tmem + C::O_COL + lane_off + c0, o);
           tmem_ld_wait();
         } else {
 #pragma unroll
@@ -423,7 +473,7 @@ __global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
           dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
       }
-      if (i < L) p.lse[((int64_t)b * Hq + h) * L + i] = l > 0.f ? m_used + __log2f(l) : -INFINITY;
+      if (i < L) p.lse[((int64_t)b * Hq + h) * L + i] = l > 0.f ? rs.m_used + __log2f(l) : -INFINITY;
       if (have_o) {
         tc_fence_before();
         mbar_arrive(&bar_o_free);
@@ -446,7 +496,7 @@ cudaError_t launch_fwd_tc(const FwdParams& p0, cudaStream_t st, int* err) {
   using C = FwdCfg<D>;
   FwdParams p = p0;
   const int S = p.S;
-  int sb = S <= 0 ? 16 : ((S < 128 ? S : 128) + 15) / 16 * 16;
+  const int sb = S <= 0 ? 16 : ((S < 64 ? S : 64) + 15) / 16 * 16;
   p.sink_box = sb;
   FwdTmaps tm;
   bool ok = make_tmap_bhld(&tm.q, p.q, p.B, p.Hq, p.L, D, p.sq.b, p.sq.h, p.sq.l, C::CW, C::BM) &&
