@@ -116,6 +116,17 @@ size_t delta_bytes(const SwaProblem& p) {
   return (n + 255) & ~(size_t)255;
 }
 
+swa::SinkSplit split_of(const SwaProblem& p) {
+  return swa::sink_split(p.seq_len, effective_window(p.window_size), p.sink_size,
+                         p.n_q_heads / p.n_kv_heads);
+}
+
+size_t partial_bytes(const SwaProblem& p) {
+  const swa::SinkSplit ss = split_of(p);
+  size_t n = (size_t)swa::sink_partial_floats(ss, p.batch, p.n_kv_heads, p.head_dim) * sizeof(float);
+  return (n + 255) & ~(size_t)255;
+}
+
 int build_bwd(const SwaBwdArgs* a, swa::BwdParams* kp) {
   if (!a) return SWA_ERR_INVALID_ARG;
   int st = check_problem(a->p);
@@ -139,6 +150,9 @@ int build_bwd(const SwaBwdArgs* a, swa::BwdParams* kp) {
   kp->W = effective_window(p.window_size); kp->S = p.sink_size;
   kp->scale = p.softmax_scale;
   kp->scale_log2 = p.softmax_scale * swa::kLog2e;
+  const swa::SinkSplit ss = split_of(p);
+  kp->part = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + delta_bytes(p));
+  kp->nst = ss.nst; kp->sp = ss.sp; kp->nc = ss.nc; kp->ch = ss.ch;
   return SWA_OK;
 }
 
@@ -178,7 +192,8 @@ int swa_check_device(void* stream) {
 
 size_t swa_bwd_workspace_size(const SwaProblem* p) {
   if (!p) return 0;
-  return delta_bytes(*p);
+  if (check_problem(*p) != SWA_OK) return delta_bytes(*p);
+  return delta_bytes(*p) + partial_bytes(*p);
 }
 
 int swa_fwd(const SwaFwdArgs* a, void* stream) {

@@ -198,7 +198,12 @@ __global__ void __launch_bounds__(128) bwd_dkdv_mma_kernel(BwdParams p) {
   float* lse_s = reinterpret_cast<float*>(dOs + 2 * BM * PITCH);  // [2][BM]
   float* dl_s = lse_s + 2 * BM;                                    // [2][BM]
 
-  const int kt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  // blocks [0, nst * nc): far chunks of the sink tiles; then one block per key tile
+  const int n_far = p.nst * p.nc;
+  const bool far = (int)blockIdx.x < n_far;
+  const int kt = far ? (int)blockIdx.x / p.nc : (int)blockIdx.x - n_far;
+  const int chunk = far ? (int)blockIdx.x % p.nc : 0;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int L = p.L, W = p.W, S = p.S;
   const int G = p.Hq / p.Hkv;
@@ -207,12 +212,30 @@ __global__ void __launch_bounds__(128) bwd_dkdv_mma_kernel(BwdParams p) {
   const T* kg = static_cast<const T*>(p.k) + b * p.sk.b + kvh * p.sk.h;
   const T* vg = static_cast<const T*>(p.v) + b * p.sv.b + kvh * p.sv.h;
 
-  int qt_lo, qt_hi;
-  query_range(k0, BN, BM, L, W, S, &qt_lo, &qt_hi);
-  const int n_qt = qt_hi - qt_lo;
-  const int n_iter = G * n_qt;
+  const bool sink_tile = kt < p.nst;
+  int qt_lo, qt_hi, it0 = 0, it1;
+  if (far) {
+    // query tiles that see only this tile's sink rows, split into chunks of ch steps
+    const int n_qt_all = (L + BM - 1) / BM;
+    qt_lo = max(near_qt_hi(kt, L, W), kt);
+    qt_hi = n_qt_all;
+    const int total = G * (qt_hi - qt_lo);
+    it0 = chunk * p.ch;
+    it1 = min(total, it0 + p.ch);
+    if (it0 >= it1) return;  // this tile has fewer chunks than the widest sink tile
+  } else if (sink_tile) {
+    qt_lo = kt;
+    qt_hi = max(near_qt_hi(kt, L, W), kt);
+    it1 = G * (qt_hi - qt_lo);
+  } else {
+    query_range(k0, BN, BM, L, W, S, &qt_lo, &qt_hi);
+    it1 = G * (qt_hi - qt_lo);
+  }
+  const int n_qt = max(qt_hi - qt_lo, 1);
+  const int n_iter = it1 - it0;
 
-  auto issue = [&](int it, int buf) {
+  auto issue = [&](int itl, int buf) {
+    const int it = it0 + itl;
     const int gi = it / n_qt, qt = qt_lo + it % n_qt;
     const int h = kvh * G + gi;
     const int q0 = qt * BM;
@@ -254,7 +277,7 @@ __global__ void __launch_bounds__(128) bwd_dkdv_mma_kernel(BwdParams p) {
       cp_async_wait<0>();
     }
     __syncthreads();
-    const int q0 = (qt_lo + it % n_qt) * BM;
+    const int q0 = (qt_lo + (it0 + it) % n_qt) * BM;
     if (!block_none_visible(q0, q0 + BM, kw0, kw0 + 16, W, S, L)) {
       const T* Qb = Qs + buf * BM * PITCH;
       const T* dOb = dOs + buf * BM * PITCH;
@@ -329,10 +352,27 @@ __global__ void __launch_bounds__(128) bwd_dkdv_mma_kernel(BwdParams p) {
 
   T* dkg = static_cast<T*>(p.dk) + b * p.sdk.b + kvh * p.sdk.h;
   T* dvg = static_cast<T*>(p.dv) + b * p.sdv.b + kvh * p.sdv.h;
+  // sink rows of a sink tile go to fp32 partial slot (far ? 1 + chunk : 0)
+  float* part_k = nullptr;
+  if (sink_tile) {
+    const int slot = far ? 1 + chunk : 0;
+    part_k = p.part + ((((int64_t)slot * p.B + b) * p.Hkv + kvh) * p.nst + kt) * 2 * p.sp * D;
+  }
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const int j = kw0 + g + r * 8;
     if (j >= L) continue;
+    if (sink_tile && j < S) {
+      float* pk = part_k + (int64_t)(j - k0) * D;
+      float* pv = pk + (int64_t)p.sp * D;
+#pragma unroll
+      for (int dn = 0; dn < D / 8; ++dn) {
+        *reinterpret_cast<float2*>(pk + dn * 8 + 2 * c) = make_float2(dk[dn][2 * r], dk[dn][2 * r + 1]);
+        *reinterpret_cast<float2*>(pv + dn * 8 + 2 * c) = make_float2(dv[dn][2 * r], dv[dn][2 * r + 1]);
+      }
+      continue;
+    }
+    if (far) continue;
     T* krow = dkg + (int64_t)j * p.sdk.l;
     T* vrow = dvg + (int64_t)j * p.sdv.l;
 #pragma unroll
@@ -343,6 +383,36 @@ __global__ void __launch_bounds__(128) bwd_dkdv_mma_kernel(BwdParams p) {
           Pack<T>::pack(dv[dn][2 * r], dv[dn][2 * r + 1]);
     }
   }
+}
+
+// Sink rows: dK = scale * sum of partials, dV = sum, added in slot order (deterministic).
+template <typename T, int D>
+__global__ void __launch_bounds__(256) bwd_sink_reduce_kernel(BwdParams p) {
+  const int64_t n = (int64_t)p.B * p.Hkv * p.nst * p.sp * D;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n) return;
+  const int d = (int)(idx % D);
+  int64_t rest = idx / D;
+  const int r = (int)(rest % p.sp);
+  rest /= p.sp;
+  const int kt = (int)(rest % p.nst);
+  rest /= p.nst;
+  const int kvh = (int)(rest % p.Hkv);
+  const int b = (int)(rest / p.Hkv);
+  const int j = kt * kSplitTile + r;
+  if (j >= p.S || j >= p.L) return;
+  const int G = p.Hq / p.Hkv;
+  const int slots = 1 + (far_steps(kt, p.L, p.W, G) + p.ch - 1) / p.ch;
+  float sk = 0.f, sv = 0.f;
+  for (int s = 0; s < slots; ++s) {
+    const float* pk = p.part + ((((int64_t)s * p.B + b) * p.Hkv + kvh) * p.nst + kt) * 2 * p.sp * D;
+    sk += pk[(int64_t)r * D + d];
+    sv += pk[(int64_t)(p.sp + r) * D + d];
+  }
+  T* dk = static_cast<T*>(p.dk) + b * p.sdk.b + kvh * p.sdk.h + (int64_t)j * p.sdk.l + d;
+  T* dv = static_cast<T*>(p.dv) + b * p.sdv.b + kvh * p.sdv.h + (int64_t)j * p.sdv.l + d;
+  *dk = Pack<T>::from(sk * p.scale);
+  *dv = Pack<T>::from(sv);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -378,8 +448,12 @@ cudaError_t launch_bwd_dkdv_mma(const BwdParams& p, cudaStream_t st) {
   auto kern = bwd_dkdv_mma_kernel<T, D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  dim3 grid((p.L + BN - 1) / BN, p.Hkv, p.B);
+  dim3 grid((p.L + BN - 1) / BN + p.nst * p.nc, p.Hkv, p.B);
   kern<<<grid, 128, smem, st>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || p.nst == 0) return e;
+  const int64_t n = (int64_t)p.B * p.Hkv * p.nst * p.sp * D;
+  bwd_sink_reduce_kernel<T, D><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p);
   return cudaGetLastError();
 }
 

@@ -87,6 +87,69 @@ __device__ __forceinline__ void query_range(int k0, int BN, int BM, int L, int W
 }
 
 // ---------------------------------------------------------------------------------------
+// Sink-key split of the dK/dV pass (64-key tiles, 64-row query tiles).
+//
+// A key tile that holds sink keys (j < S) receives gradient from every later query, which
+// would make its CTA do ~L/64 * G query-tile steps while every other tile does a handful.
+// Its work is therefore cut in two: the "near" query tiles (those that also see the tile
+// through the window) stay with the tile's own CTA; the "far" ones, which see only the sink
+// rows, are spread over `nc` chunk CTAs of at most `ch` (query head, query tile) steps each.
+// Every such CTA writes fp32 partial sums of the sink rows to the workspace, and a reduction
+// adds them in a fixed order (deterministic).
+// ---------------------------------------------------------------------------------------
+struct SinkSplit {
+  int nst;  // key tiles that hold sinks
+  int sp;   // rows kept per sink tile in the partials (multiple of 16, <= 64)
+  int nc;   // far chunks per sink tile (the maximum over the sink tiles)
+  int ch;   // far (query head, query tile) steps per chunk
+};
+
+constexpr int kSplitTile = 64;       // key and query tile size of the dK/dV pass
+constexpr int kSplitChunkSteps = 64; // steps per far chunk
+
+// First query tile past the tile's window range: [k0/64, near_hi) see keys of the tile
+// through the window; later query tiles see only its sink keys.
+__host__ __device__ inline int near_qt_hi(int kt, int L, int W) {
+  const int n_qt = (L + kSplitTile - 1) / kSplitTile;
+  const int k0 = kt * kSplitTile;
+  const int lo = k0 / kSplitTile;
+  if (W <= 0) return lo;
+  const int k_last = (k0 + kSplitTile < L ? k0 + kSplitTile : L) - 1;
+  long long last_row = (long long)k_last + W - 1;
+  if (last_row > L - 1) last_row = L - 1;
+  const int hi = (int)(last_row / kSplitTile) + 1;
+  return hi < n_qt ? hi : n_qt;
+}
+
+__host__ __device__ inline int far_steps(int kt, int L, int W, int G) {
+  const int n_qt = (L + kSplitTile - 1) / kSplitTile;
+  const int lo = near_qt_hi(kt, L, W);
+  const int first = kt;  // query tiles before the key tile see none of it
+  const int start = lo > first ? lo : first;
+  return start < n_qt ? G * (n_qt - start) : 0;
+}
+
+__host__ __device__ inline SinkSplit sink_split(int L, int W, int S, int G) {
+  SinkSplit ss;
+  const int sk = S < L ? S : L;
+  ss.nst = sk > 0 ? (sk + kSplitTile - 1) / kSplitTile : 0;
+  const int s16 = (S + 15) / 16 * 16;
+  ss.sp = s16 < kSplitTile ? s16 : kSplitTile;
+  ss.ch = kSplitChunkSteps;
+  ss.nc = 0;
+  for (int kt = 0; kt < ss.nst; ++kt) {
+    const int c = (far_steps(kt, L, W, G) + ss.ch - 1) / ss.ch;
+    if (c > ss.nc) ss.nc = c;
+  }
+  return ss;
+}
+
+// Floats of sink partials: (1 + nc) slots x B x Hkv x nst tiles x {dK, dV} x sp rows x D.
+__host__ __device__ inline long long sink_partial_floats(const SinkSplit& ss, int B, int Hkv, int D) {
+  return (long long)(1 + ss.nc) * B * Hkv * ss.nst * 2 * ss.sp * D;
+}
+
+// ---------------------------------------------------------------------------------------
 // Element types
 // ---------------------------------------------------------------------------------------
 template <typename T> struct Pack;

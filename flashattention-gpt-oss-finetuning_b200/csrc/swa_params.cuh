@@ -35,6 +35,8 @@ struct BwdParams {
   int B, Hq, Hkv, L, W, S;
   float scale;       // softmax_scale
   float scale_log2;  // softmax_scale * log2(e)
+  float* part;       // sink-row partial sums of dK / dV (workspace, after delta)
+  int nst, sp, nc, ch;  // SinkSplit
 };
 
 }  // namespace swa
