@@ -13,7 +13,7 @@ namespace swa {
 template <typename T, int D> cudaError_t launch_fwd_tc(const FwdParams&, cudaStream_t, int*);
 template <typename T, int D> cudaError_t launch_bwd_preprocess(const BwdParams&, cudaStream_t);
 template <typename T, int D> cudaError_t launch_bwd_dq_mma(const BwdParams&, cudaStream_t);
-template <typename T, int D> cudaError_t launch_bwd_dkdv_mma(const BwdParams&, cudaStream_t);
+template <typename T, int D> cudaError_t launch_bwd_dkdv_tc(const BwdParams&, cudaStream_t, int*);
 }  // namespace swa
 
 namespace {
@@ -74,7 +74,9 @@ int check_tensor(const SwaTensor& t, bool need_ptr) {
 
 swa::Strides strides(const SwaTensor& t) { return {t.stride_b, t.stride_h, t.stride_l}; }
 
-int effective_window(int w) { return w < 0 ? 0 : w; }
+// W <= 0: only sinks visible; W >= L: plain causal (every window test passes), so W is
+// clamped to L, which also keeps index arithmetic such as j + W inside int range.
+int effective_window(int w, int L) { return w < 0 ? 0 : (w > L ? (L > 0 ? L : 1) : w); }
 
 template <template <typename, int> class F, typename P>
 int dispatch(const SwaProblem& pr, const P& kp, cudaStream_t st) {
@@ -108,7 +110,9 @@ template <typename T, int D> struct Dq {
   static cudaError_t run(const swa::BwdParams& p, cudaStream_t s) { return swa::launch_bwd_dq_mma<T, D>(p, s); }
 };
 template <typename T, int D> struct Dkdv {
-  static cudaError_t run(const swa::BwdParams& p, cudaStream_t s) { return swa::launch_bwd_dkdv_mma<T, D>(p, s); }
+  static cudaError_t run(const swa::BwdParams& p, cudaStream_t s) {
+    return swa::launch_bwd_dkdv_tc<T, D>(p, s, device_error_ptr());
+  }
 };
 
 size_t delta_bytes(const SwaProblem& p) {
@@ -117,8 +121,8 @@ size_t delta_bytes(const SwaProblem& p) {
 }
 
 swa::SinkSplit split_of(const SwaProblem& p) {
-  return swa::sink_split(p.seq_len, effective_window(p.window_size), p.sink_size,
-                         p.n_q_heads / p.n_kv_heads);
+  return swa::sink_split(p.seq_len, effective_window(p.window_size, p.seq_len), p.sink_size,
+                         p.n_q_heads / p.n_kv_heads, swa::kDkdvKeyTile, swa::kDkdvQueryTile);
 }
 
 size_t partial_bytes(const SwaProblem& p) {
@@ -147,12 +151,13 @@ int build_bwd(const SwaBwdArgs* a, swa::BwdParams* kp) {
   kp->sq = strides(a->q); kp->sk = strides(a->k); kp->sv = strides(a->v); kp->so = strides(a->o);
   kp->sdo = strides(a->dout); kp->sdq = strides(a->dq); kp->sdk = strides(a->dk); kp->sdv = strides(a->dv);
   kp->B = p.batch; kp->Hq = p.n_q_heads; kp->Hkv = p.n_kv_heads; kp->L = p.seq_len;
-  kp->W = effective_window(p.window_size); kp->S = p.sink_size;
+  kp->W = effective_window(p.window_size, p.seq_len); kp->S = p.sink_size;
   kp->scale = p.softmax_scale;
   kp->scale_log2 = p.softmax_scale * swa::kLog2e;
   const swa::SinkSplit ss = split_of(p);
   kp->part = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + delta_bytes(p));
   kp->nst = ss.nst; kp->sp = ss.sp; kp->nc = ss.nc; kp->ch = ss.ch;
+  kp->bn_split = ss.bn; kp->bm_split = ss.bm;
   return SWA_OK;
 }
 
@@ -210,7 +215,7 @@ int swa_fwd(const SwaFwdArgs* a, void* stream) {
   kp.q = a->q.ptr; kp.k = a->k.ptr; kp.v = a->v.ptr; kp.o = a->o.ptr; kp.lse = a->lse;
   kp.sq = strides(a->q); kp.sk = strides(a->k); kp.sv = strides(a->v); kp.so = strides(a->o);
   kp.B = a->p.batch; kp.Hq = a->p.n_q_heads; kp.Hkv = a->p.n_kv_heads; kp.L = a->p.seq_len;
-  kp.W = effective_window(a->p.window_size); kp.S = a->p.sink_size;
+  kp.W = effective_window(a->p.window_size, a->p.seq_len); kp.S = a->p.sink_size;
   kp.scale_log2 = a->p.softmax_scale * swa::kLog2e;
   return dispatch<Fwd>(a->p, kp, static_cast<cudaStream_t>(stream));
 }

@@ -1,0 +1,486 @@
+// swa_bwd_tc.cu -- dK/dV kernel on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Persistent kernel.  A work item is one 128-key tile of one (batch, KV head) together with a
+// range of (query head of the GQA group, 64-row query tile) steps: for an ordinary tile, every
+// query tile that sees it through the window; for a tile holding sink keys, those plus, in
+// separate "far chunk" items, the query tiles that see only its sinks (see SinkSplit).
+// dK and dV of the tile accumulate in TMEM over all steps of the item and are written once:
+// deterministic, no atomics (the reference accumulates them with fp32 atomic_add,
+// flash_attention_gpt_oss.py:295-304, 323-332).
+//
+// Per step, with K, V [128 keys x D] resident in shared memory and Q, dO [64 rows x D]
+// streamed by TMA:
+//   S^T  = K Q^T      (M=128 keys, N=64 rows)  -> TMEM   (tcgen05.mma, A and B K-major smem)
+//   dP^T = V dO^T                               -> TMEM
+//   P^T  = 2^(S^T * scale*log2e - LSE_row), masked;  dS^T = P^T (dP^T - Delta_row)
+//          (warps 4..11; each thread owns one key row and 32 query columns)  -> TMEM, 16-bit
+//   dV  += P^T dO     (A = P^T from TMEM, B = dO MN-major smem)
+//   dK  += dS^T Q     (A = dS^T from TMEM, B = Q MN-major smem)
+// S^T / dP^T / P^T / dS^T are double-buffered (head dims <= 64) so the MMAs of step t+1 run
+// while the elementwise warps work on step t.
+//
+// Warp roles (12 warps, 384 threads): warp 0 TMA producer (K/V per item, Q/dO + LSE/Delta per
+// step), warp 1 MMA issuer (one thread), warps 4..11 elementwise + epilogue.
+// Every mbarrier wait is bounded; a wait that gives up records an error and the CTA exits.
+#include <type_traits>
+
+#include "sm100.cuh"
+#include "swa_common.cuh"
+#include "swa_params.cuh"
+#include "tma_host.h"
+
+namespace swa {
+using namespace sm100;
+
+struct DkdvTmaps {
+  CUtensorMap q, dout, k, v;
+};
+
+template <int D>
+struct DkdvCfg {
+  static constexpr int BN = 128, BM = 64;  // key tile (MMA M), query tile (MMA N)
+  static constexpr int CW = D < 64 ? D : 64;
+  static constexpr int NCH = D / CW;
+  static constexpr int ROWB = CW * 2;
+  static constexpr uint32_t SWZ = CW == 64 ? kSw128 : (CW == 32 ? kSw64 : kSw32);
+  static constexpr int KV_BYTES = BN * D * 2;
+  static constexpr int QT_BYTES = BM * D * 2;
+  static constexpr int STAGE = 2 * QT_BYTES + 1024;  // Q, dO, then LSE[64], Delta[64]
+  static constexpr int NKV = D <= 64 ? 2 : 1;        // K/V buffers (items in flight)
+  static constexpr int NST = D <= 64 ? 4 : 3;        // Q/dO stages
+  static constexpr int NB = D <= 64 ? 2 : 1;         // TMEM buffers of S^T, dP^T, P^T, dS^T
+  static constexpr int SMEM = 1024 + NKV * 2 * KV_BYTES + NST * STAGE;
+  static constexpr int S_COL = 0, DP_COL = 64 * NB, P_COL = 128 * NB, DS_COL = 160 * NB;
+  static constexpr int DK_COL = 192 * NB, DV_COL = 192 * NB + D;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr int THREADS = 384;
+};
+
+struct DkdvItem {
+  int b, kvh, kt, chunk;  // chunk < 0: the tile's own item
+  int qt_lo, n_qtr;       // query tiles [qt_lo, qt_lo + n_qtr)
+  int it0, n;             // steps [it0, it0 + n) of G * n_qtr
+};
+
+__device__ __forceinline__ DkdvItem dkdv_item(int idx, const BwdParams& p, int G, int n_kt, int n_qt) {
+  DkdvItem it;
+  const int n_far = p.B * p.Hkv * p.nst * p.nc;
+  if (idx < n_far) {
+    int r = idx;
+    it.chunk = r % p.nc;
+    r /= p.nc;
+    it.kt = r % p.nst;
+    r /= p.nst;
+    it.kvh = r % p.Hkv;
+    it.b = r / p.Hkv;
+    it.qt_lo = far_qt_lo(it.kt, p.L, p.W, 128, 64);
+    it.n_qtr = n_qt - it.qt_lo;
+    const int total = it.n_qtr > 0 ? G * it.n_qtr : 0;
+    it.it0 = it.chunk * p.ch;
+    const int end = min(total, it.it0 + p.ch);
+    it.n = end > it.it0 ? end - it.it0 : 0;
+  } else {
+    int r = idx - n_far;
+    it.chunk = -1;
+    it.kt = r % n_kt;
+    r /= n_kt;
+    it.kvh = r % p.Hkv;
+    it.b = r / p.Hkv;
+    const int first = it.kt * 2;
+    it.qt_lo = first;
+    it.n_qtr = max(near_qt_hi(it.kt, p.L, p.W, 128, 64), first) - first;
+    it.it0 = 0;
+    it.n = G * it.n_qtr;
+  }
+  return it;
+}
+
+__device__ __forceinline__ void record_err(int* err) {
+  if (err) atomicCAS(err, 0, 1);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(384, 1) bwd_dkdv_tc_kernel(const __grid_constant__ DkdvTmaps tm,
+                                                             const BwdParams p, int* err) {
+  using C = DkdvCfg<D>;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* KVs = smem;                                // [NKV][K, V]
+  unsigned char* STs = smem + C::NKV * 2 * C::KV_BYTES;     // [NST][Q, dO, lse, delta]
+
+  __shared__ uint64_t bar_kv_full[C::NKV], bar_kv_empty[C::NKV];
+  __shared__ uint64_t bar_full[C::NST], bar_empty[C::NST];
+  __shared__ uint64_t bar_s[C::NB], bar_p[C::NB], bar_acc, bar_acc_free;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_sh;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int L = p.L, W = p.W, S = p.S;
+  const int G = p.Hq / p.Hkv;
+  const int n_kt = (L + 127) / 128;
+  const int n_qt = (L + 63) / 64;
+  const int n_items = p.B * p.Hkv * (p.nst * p.nc + n_kt);
+  const bool dead = err != nullptr && *reinterpret_cast<volatile int*>(err) != 0;
+
+  if (threadIdx.x == 0) {
+    abort_sh = dead ? 1 : 0;
+    for (int s = 0; s < C::NKV; ++s) {
+      mbar_init(&bar_kv_full[s], 1);
+      mbar_init(&bar_kv_empty[s], 1);
+    }
+    for (int s = 0; s < C::NST; ++s) {
+      mbar_init(&bar_full[s], 1);
+      mbar_init(&bar_empty[s], 1);
+    }
+    for (int s = 0; s < C::NB; ++s) {
+      mbar_init(&bar_s[s], 1);
+      mbar_init(&bar_p[s], 256);
+    }
+    mbar_init(&bar_acc, 1);
+    mbar_init(&bar_acc_free, 256);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer (whole warp)
+    if (!dead) {
+      if (lane == 0) {
+        tma_prefetch_desc(&tm.q);
+        tma_prefetch_desc(&tm.dout);
+        tma_prefetch_desc(&tm.k);
+        tma_prefetch_desc(&tm.v);
+      }
+      int qi = 0, gs = 0;
+      bool ok = true;
+      for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+        const DkdvItem itm = dkdv_item(idx, p, G, n_kt, n_qt);
+        if (itm.n == 0) continue;
+        const int kvb = qi % C::NKV;
+        if (qi >= C::NKV && !(ok = mbar_wait(&bar_kv_empty[kvb], ((qi / C::NKV) - 1) & 1, &abort_sh))) break;
+        if (lane == 0) {
+          unsigned char* Kb = KVs + kvb * 2 * C::KV_BYTES;
+          mbar_arrive_expect_tx(&bar_kv_full[kvb], 2 * C::KV_BYTES);
+#pragma unroll
+          for (int c = 0; c < C::NCH; ++c) {
+            tma_load_4d(Kb + c * 128 * C::ROWB, &tm.k, &bar_kv_full[kvb], c * C::CW, itm.kt * 128, itm.kvh, itm.b);
+            tma_load_4d(Kb + C::KV_BYTES + c * 128 * C::ROWB, &tm.v, &bar_kv_full[kvb], c * C::CW, itm.kt * 128,
+                        itm.kvh, itm.b);
+          }
+        }
+        for (int t = 0; t < itm.n; ++t, ++gs) {
+          const int st = gs % C::NST;
+          if (gs >= C::NST && !(ok = mbar_wait(&bar_empty[st], ((gs / C::NST) - 1) & 1, &abort_sh))) break;
+          const int it = itm.it0 + t;
+          const int h = itm.kvh * G + it / itm.n_qtr;
+          const int q0 = (itm.qt_lo + it % itm.n_qtr) * 64;
+          unsigned char* Sb = STs + st * C::STAGE;
+          float* lse_s = reinterpret_cast<float*>(Sb + 2 * C::QT_BYTES);
+          const int64_t rb = ((int64_t)itm.b * p.Hq + h) * L;
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int i = q0 + k * 32 + lane;
+            lse_s[k * 32 + lane] = i < L ? p.lse[rb + i] : INFINITY;
+            lse_s[64 + k * 32 + lane] = i < L ? p.delta[rb + i] : 0.f;
+          }
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&bar_full[st], 2 * C::QT_BYTES);
+#pragma unroll
+            for (int c = 0; c < C::NCH; ++c) {
+              tma_load_4d(Sb + c * 64 * C::ROWB, &tm.q, &bar_full[st], c * C::CW, q0, h, itm.b);
+              tma_load_4d(Sb + C::QT_BYTES + c * 64 * C::ROWB, &tm.dout, &bar_full[st], c * C::CW, q0, h, itm.b);
+            }
+          }
+        }
+        ++qi;
+      }
+      if (!ok) {
+        abort_sh = 1;
+        record_err(err);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0 && !dead) {
+      constexpr uint32_t id_s = idesc_f16(128, 64, kBf16, false, false);  // S^T, dP^T
+      constexpr uint32_t id_a = idesc_f16(128, D, kBf16, false, true);    // dV, dK
+      int qi = 0, gs = 0;
+      bool ok = true;
+      for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+        const DkdvItem itm = dkdv_item(idx, p, G, n_kt, n_qt);
+        if (itm.n == 0) continue;
+        const int kvb = qi % C::NKV;
+        if (!(ok = mbar_wait(&bar_kv_full[kvb], (qi / C::NKV) & 1, &abort_sh))) break;
+        const unsigned char* Kb = KVs + kvb * 2 * C::KV_BYTES;
+        const unsigned char* Vb = Kb + C::KV_BYTES;
+        const int g0 = gs;  // global index of the item's first step
+        int next = 0;       // next step of this item whose dV/dK MMAs are due
+        auto dvdk = [&](int u) -> bool {
+          const int gu = g0 + u;
+          const int bb = gu % C::NB;
+          if (!mbar_wait(&bar_p[bb], (gu / C::NB) & 1, &abort_sh)) return false;
+          // the previous item's epilogue must have read dK/dV before they are overwritten
+          if (u == 0 && qi > 0 && !mbar_wait(&bar_acc_free, (qi - 1) & 1, &abort_sh)) return false;
+          tc_fence_after();
+          const int st = gu % C::NST;
+          const unsigned char* Qb = STs + st * C::STAGE;
+          const unsigned char* dOb = Qb + C::QT_BYTES;
+          const uint32_t tP = tmem + C::P_COL + bb * 32, tdS = tmem + C::DS_COL + bb * 32;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {  // K = 64 query rows, 16 per MMA
+            const uint64_t bdo = sdesc(saddr(dOb + ks * 16 * C::ROWB), 64 * C::ROWB, 8 * C::ROWB, C::SWZ);
+            const uint64_t bq = sdesc(saddr(Qb + ks * 16 * C::ROWB), 64 * C::ROWB, 8 * C::ROWB, C::SWZ);
+            const uint32_t acc = (u > 0 || ks > 0) ? 1u : 0u;
+            mma_ts(tmem + C::DV_COL, tP + ks * 8, bdo, id_a, acc);
+            mma_ts(tmem + C::DK_COL, tdS + ks * 8, bq, id_a, acc);
+          }
+          mma_commit(&bar_empty[st]);
+          return true;
+        };
+        for (int t = 0; t < itm.n && ok; ++t) {
+          // free the TMEM buffer that step t will use
+          while (ok && next <= t - C::NB) ok = dvdk(next++);
+          if (!ok) break;
+          const int gt = g0 + t;
+          const int st = gt % C::NST, bb = gt % C::NB;
+          if (!(ok = mbar_wait(&bar_full[st], (gt / C::NST) & 1, &abort_sh))) break;
+          tc_fence_after();
+          const unsigned char* Qb = STs + st * C::STAGE;
+          const unsigned char* dOb = Qb + C::QT_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks) {
+            const int ch = (ks * 16) / C::CW, within = (ks * 16) % C::CW;
+            const uint64_t ak = sdesc(saddr(Kb + ch * 128 * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
+            const uint64_t av = sdesc(saddr(Vb + ch * 128 * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
+            const uint64_t bq = sdesc(saddr(Qb + ch * 64 * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
+            const uint64_t bdo = sdesc(saddr(dOb + ch * 64 * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
+            mma_ss(tmem + C::S_COL + bb * 64, ak, bq, id_s, ks > 0 ? 1u : 0u);
+            mma_ss(tmem + C::DP_COL + bb * 64, av, bdo, id_s, ks > 0 ? 1u : 0u);
+          }
+          mma_commit(&bar_s[bb]);
+          if (t == itm.n - 1) mma_commit(&bar_kv_empty[kvb]);  // last read of K/V
+          while (ok && next <= t - 1) ok = dvdk(next++);
+        }
+        while (ok && next < itm.n) ok = dvdk(next++);
+        if (!ok) break;
+        mma_commit(&bar_acc);
+        gs += itm.n;
+        ++qi;
+      }
+      if (!ok) {
+        abort_sh = 1;
+        record_err(err);
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ elementwise + epilogue
+    const int quad = warp & 3, half = (warp - 4) >> 2;
+    const int r = quad * 32 + lane;  // key row of the tile (TMEM lane)
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const float sl2 = p.scale_log2;
+    int qi = 0, gs = 0;
+    bool ok = !dead;
+    for (int idx = blockIdx.x; idx < n_items; idx += gridDim.x) {
+      const DkdvItem itm = dkdv_item(idx, p, G, n_kt, n_qt);
+      if (itm.n == 0 && itm.chunk >= 0) continue;  // empty far chunk: not part of the sums
+      const int k0 = itm.kt * 128;
+      const int j = k0 + r;
+      const int kw0 = k0 + quad * 32;  // this warp's 32 keys
+      for (int t = 0; t < itm.n && ok; ++t) {
+        const int gt = gs + t;
+        const int bb = gt % C::NB, st = gt % C::NST;
+        if (!(ok = mbar_wait(&bar_s[bb], (gt / C::NB) & 1, &abort_sh))) break;
+        tc_fence_after();
+        const int it = itm.it0 + t;
+        const int qc0 = (itm.qt_lo + it % itm.n_qtr) * 64 + half * 32;  // first query column
+        const uint32_t tP = tmem + C::P_COL + bb * 32 + half * 16 + lane_off;
+        const uint32_t tdS = tmem + C::DS_COL + bb * 32 + half * 16 + lane_off;
+        if (block_none_visible(qc0, qc0 + 32, kw0, kw0 + 32, W, S, L)) {
+          const uint32_t z[16] = {0u};
+          tmem_st16(tP, z);
+          tmem_st16(tdS, z);
+        } else {
+          const bool full = block_all_visible(qc0, qc0 + 32, kw0, kw0 + 32, W, S, L);
+          float s[32], dp[32];
+          tmem_ld32(tmem + C::S_COL + bb * 64 + half * 32 + lane_off, reinterpret_cast<uint32_t*>(s));
+          tmem_ld32(tmem + C::DP_COL + bb * 64 + half * 32 + lane_off, reinterpret_cast<uint32_t*>(dp));
+          const float* lse_s = reinterpret_cast<const float*>(STs + st * C::STAGE + 2 * C::QT_BYTES) + half * 32;
+          const float* dl_s = lse_s + 64;
+          tmem_ld_wait();
+          // query i = qc0 + c sees key j iff c >= c_min and (c < c_max or j < S)
+          const int c_min = j - qc0;
+          const int c_max = (W > 0 && j >= S) ? j + W - qc0 : (j < S ? 1 << 30 : -(1 << 30));
+          uint32_t pw[16], dw[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            float pv[2], dv[2];
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              const int c = 2 * e + h2;
+              float pr = fast_exp2(fmaf(s[c], sl2, -lse_s[c]));
+              if (!full) pr = (c >= c_min && c < c_max) ? pr : 0.f;
+              pv[h2] = pr;
+              dv[h2] = pr * (dp[c] - dl_s[c]);
+            }
+            pw[e] = Pack<T>::pack(pv[0], pv[1]);
+            dw[e] = Pack<T>::pack(dv[0], dv[1]);
+          }
+          tmem_st16(tP, pw);
+          tmem_st16(tdS, dw);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&bar_p[bb]);
+      }
+      // ---- epilogue: this thread writes columns [half*D/2, (half+1)*D/2) of key row j
+      const bool have = itm.n > 0 && ok;
+      if (have) {
+        ok = mbar_wait(&bar_acc, qi & 1, &abort_sh);
+        tc_fence_after();
+      }
+      const bool sink_row = itm.kt < p.nst && j < S;
+      float* part = nullptr;
+      if (itm.kt < p.nst) {
+        const int slot = itm.chunk >= 0 ? 1 + itm.chunk : 0;
+        part = p.part + ((((int64_t)slot * p.B + itm.b) * p.Hkv + itm.kvh) * p.nst + itm.kt) * 2 * p.sp * D;
+      }
+      const bool write_final = itm.chunk < 0 && !sink_row && j < L;
+      const bool write_part = sink_row && j < L;
+      T* dkr = static_cast<T*>(p.dk) + itm.b * p.sdk.b + itm.kvh * p.sdk.h + (int64_t)j * p.sdk.l;
+      T* dvr = static_cast<T*>(p.dv) + itm.b * p.sdv.b + itm.kvh * p.sdv.h + (int64_t)j * p.sdv.l;
+#pragma unroll
+      for (int c0 = half * (D / 2); c0 < (half + 1) * (D / 2); c0 += 8) {
+        uint32_t ka[8], va[8];
+        if (have && ok) {
+          // 32x32b.x8 loads (8 columns) keep the loop uniform for every head dim
+          asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                       : "=r"(ka[0]), "=r"(ka[1]), "=r"(ka[2]), "=r"(ka[3]), "=r"(ka[4]), "=r"(ka[5]),
+                         "=r"(ka[6]), "=r"(ka[7])
+                       : "r"(tmem + C::DK_COL + c0 + lane_off));
+          asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                       : "=r"(va[0]), "=r"(va[1]), "=r"(va[2]), "=r"(va[3]), "=r"(va[4]), "=r"(va[5]),
+                         "=r"(va[6]), "=r"(va[7])
+                       : "r"(tmem + C::DV_COL + c0 + lane_off));
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ka[e] = va[e] = 0u;
+        }
+        if (write_part) {
+          float* pk = part + (int64_t)(j - k0) * D + c0;
+          float* pv = pk + (int64_t)p.sp * D;
+#pragma unroll
+          for (int e = 0; e < 8; e += 4) {
+            *reinterpret_cast<float4*>(pk + e) = make_float4(__uint_as_float(ka[e]), __uint_as_float(ka[e + 1]),
+                                                             __uint_as_float(ka[e + 2]), __uint_as_float(ka[e + 3]));
+            *reinterpret_cast<float4*>(pv + e) = make_float4(__uint_as_float(va[e]), __uint_as_float(va[e + 1]),
+                                                             __uint_as_float(va[e + 2]), __uint_as_float(va[e + 3]));
+          }
+        } else if (write_final) {
+          uint32_t kw[4], vw[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            kw[e] = Pack<T>::pack(__uint_as_float(ka[2 * e]) * p.scale, __uint_as_float(ka[2 * e + 1]) * p.scale);
+            vw[e] = Pack<T>::pack(__uint_as_float(va[2 * e]), __uint_as_float(va[2 * e + 1]));
+          }
+          *reinterpret_cast<uint4*>(dkr + c0) = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+          *reinterpret_cast<uint4*>(dvr + c0) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+        }
+      }
+      if (have) {
+        tc_fence_before();
+        mbar_arrive(&bar_acc_free);
+        gs += itm.n;
+        ++qi;
+      }
+    }
+    if (!ok && !dead) {
+      abort_sh = 1;
+      record_err(err);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+// Sink rows: dK = scale * sum of partials, dV = sum, added in slot order (deterministic).
+template <typename T, int D>
+__global__ void __launch_bounds__(256) bwd_sink_reduce_kernel(BwdParams p) {
+  const int64_t n = (int64_t)p.B * p.Hkv * p.nst * p.sp * D;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n) return;
+  const int d = (int)(idx % D);
+  int64_t rest = idx / D;
+  const int r = (int)(rest % p.sp);
+  rest /= p.sp;
+  const int kt = (int)(rest % p.nst);
+  rest /= p.nst;
+  const int kvh = (int)(rest % p.Hkv);
+  const int b = (int)(rest / p.Hkv);
+  const int j = kt * p.bn_split + r;
+  if (j >= p.S || j >= p.L) return;
+  const int G = p.Hq / p.Hkv;
+  const int slots = 1 + (far_steps(kt, p.L, p.W, G, p.bn_split, p.bm_split) + p.ch - 1) / p.ch;
+  float sk = 0.f, sv = 0.f;
+  for (int s = 0; s < slots; ++s) {
+    const float* pk = p.part + ((((int64_t)s * p.B + b) * p.Hkv + kvh) * p.nst + kt) * 2 * p.sp * D;
+    sk += pk[(int64_t)r * D + d];
+    sv += pk[(int64_t)(p.sp + r) * D + d];
+  }
+  T* dk = static_cast<T*>(p.dk) + b * p.sdk.b + kvh * p.sdk.h + (int64_t)j * p.sdk.l + d;
+  T* dv = static_cast<T*>(p.dv) + b * p.sdv.b + kvh * p.sdv.h + (int64_t)j * p.sdv.l + d;
+  *dk = Pack<T>::from(sk * p.scale);
+  *dv = Pack<T>::from(sv);
+}
+
+template <typename T, int D>
+cudaError_t launch_sink_reduce(const BwdParams& p, cudaStream_t st) {
+  const int64_t n = (int64_t)p.B * p.Hkv * p.nst * p.sp * D;
+  if (n == 0) return cudaSuccess;
+  bwd_sink_reduce_kernel<T, D><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T, int D>
+cudaError_t launch_bwd_dkdv_tc(const BwdParams& p, cudaStream_t st, int* err) {
+  using C = DkdvCfg<D>;
+  DkdvTmaps tm;
+  bool ok = make_tmap_bhld(&tm.q, p.q, p.B, p.Hq, p.L, D, p.sq.b, p.sq.h, p.sq.l, C::CW, 64) &&
+            make_tmap_bhld(&tm.dout, p.dout, p.B, p.Hq, p.L, D, p.sdo.b, p.sdo.h, p.sdo.l, C::CW, 64) &&
+            make_tmap_bhld(&tm.k, p.k, p.B, p.Hkv, p.L, D, p.sk.b, p.sk.h, p.sk.l, C::CW, 128) &&
+            make_tmap_bhld(&tm.v, p.v, p.B, p.Hkv, p.L, D, p.sv.b, p.sv.h, p.sv.l, C::CW, 128);
+  if (!ok) return cudaErrorInvalidValue;
+  auto kern = bwd_dkdv_tc_kernel<T, D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e != cudaSuccess) return e;
+  const int n_kt = (p.L + 127) / 128;
+  const int n_items = p.B * p.Hkv * (p.nst * p.nc + n_kt);
+  const int grid = persistent_grid(kern, C::THREADS, C::SMEM, C::TMEM_COLS, n_items);
+  if (grid <= 0) return cudaErrorInvalidConfiguration;
+  kern<<<grid, C::THREADS, C::SMEM, st>>>(tm, p, err);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || p.nst == 0) return e;
+  return launch_sink_reduce<T, D>(p, st);
+}
+
+#define SWA_INST(T, D) template cudaError_t launch_bwd_dkdv_tc<T, D>(const BwdParams&, cudaStream_t, int*);
+SWA_INST(__half, 16) SWA_INST(__half, 32) SWA_INST(__half, 64) SWA_INST(__half, 128)
+SWA_INST(__nv_bfloat16, 16) SWA_INST(__nv_bfloat16, 32) SWA_INST(__nv_bfloat16, 64)
+SWA_INST(__nv_bfloat16, 128)
+#undef SWA_INST
+
+}  // namespace swa

@@ -99,46 +99,57 @@ __device__ __forceinline__ void query_range(int k0, int BN, int BM, int L, int W
 // ---------------------------------------------------------------------------------------
 struct SinkSplit {
   int nst;  // key tiles that hold sinks
-  int sp;   // rows kept per sink tile in the partials (multiple of 16, <= 64)
+  int sp;   // rows kept per sink tile in the partials (multiple of 16, <= key tile)
   int nc;   // far chunks per sink tile (the maximum over the sink tiles)
   int ch;   // far (query head, query tile) steps per chunk
+  int bn;   // key tile
+  int bm;   // query tile
 };
 
-constexpr int kSplitTile = 64;       // key and query tile size of the dK/dV pass
-constexpr int kSplitChunkSteps = 64; // steps per far chunk
+constexpr int kSplitChunkSteps = 64;  // steps per far chunk
+constexpr int kDkdvKeyTile = 128;     // key tile of the dK/dV pass
+constexpr int kDkdvQueryTile = 64;    // query tile of the dK/dV pass
 
-// First query tile past the tile's window range: [k0/64, near_hi) see keys of the tile
-// through the window; later query tiles see only its sink keys.
-__host__ __device__ inline int near_qt_hi(int kt, int L, int W) {
-  const int n_qt = (L + kSplitTile - 1) / kSplitTile;
-  const int k0 = kt * kSplitTile;
-  const int lo = k0 / kSplitTile;
+// First query tile (of bm rows) past the window range of key tile kt (of bn keys): query
+// tiles in [kt*bn/bm, near_qt_hi) see the tile through the window; later ones only see its
+// sink keys.
+__host__ __device__ inline int near_qt_hi(int kt, int L, int W, int bn, int bm) {
+  const int n_qt = (L + bm - 1) / bm;
+  const int k0 = kt * bn;
+  const int lo = k0 / bm;
   if (W <= 0) return lo;
-  const int k_last = (k0 + kSplitTile < L ? k0 + kSplitTile : L) - 1;
+  const int k_last = (k0 + bn < L ? k0 + bn : L) - 1;
   long long last_row = (long long)k_last + W - 1;
   if (last_row > L - 1) last_row = L - 1;
-  const int hi = (int)(last_row / kSplitTile) + 1;
+  const int hi = (int)(last_row / bm) + 1;
   return hi < n_qt ? hi : n_qt;
 }
 
-__host__ __device__ inline int far_steps(int kt, int L, int W, int G) {
-  const int n_qt = (L + kSplitTile - 1) / kSplitTile;
-  const int lo = near_qt_hi(kt, L, W);
-  const int first = kt;  // query tiles before the key tile see none of it
-  const int start = lo > first ? lo : first;
+// First query tile of the far range of key tile kt.
+__host__ __device__ inline int far_qt_lo(int kt, int L, int W, int bn, int bm) {
+  const int hi = near_qt_hi(kt, L, W, bn, bm);
+  const int first = (kt * bn) / bm;
+  return hi > first ? hi : first;
+}
+
+__host__ __device__ inline int far_steps(int kt, int L, int W, int G, int bn, int bm) {
+  const int n_qt = (L + bm - 1) / bm;
+  const int start = far_qt_lo(kt, L, W, bn, bm);
   return start < n_qt ? G * (n_qt - start) : 0;
 }
 
-__host__ __device__ inline SinkSplit sink_split(int L, int W, int S, int G) {
+__host__ __device__ inline SinkSplit sink_split(int L, int W, int S, int G, int bn, int bm) {
   SinkSplit ss;
+  ss.bn = bn;
+  ss.bm = bm;
   const int sk = S < L ? S : L;
-  ss.nst = sk > 0 ? (sk + kSplitTile - 1) / kSplitTile : 0;
+  ss.nst = sk > 0 ? (sk + bn - 1) / bn : 0;
   const int s16 = (S + 15) / 16 * 16;
-  ss.sp = s16 < kSplitTile ? s16 : kSplitTile;
+  ss.sp = s16 < bn ? s16 : bn;
   ss.ch = kSplitChunkSteps;
   ss.nc = 0;
   for (int kt = 0; kt < ss.nst; ++kt) {
-    const int c = (far_steps(kt, L, W, G) + ss.ch - 1) / ss.ch;
+    const int c = (far_steps(kt, L, W, G, bn, bm) + ss.ch - 1) / ss.ch;
     if (c > ss.nc) ss.nc = c;
   }
   return ss;

@@ -37,6 +37,7 @@ struct BwdParams {
   float scale_log2;  // softmax_scale * log2(e)
   float* part;       // sink-row partial sums of dK / dV (workspace, after delta)
   int nst, sp, nc, ch;  // SinkSplit
+  int bn_split, bm_split;  // key / query tile sizes the split was made for
 };
 
 }  // namespace swa
