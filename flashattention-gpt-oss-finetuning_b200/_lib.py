@@ -28,7 +28,7 @@ SWA_BF16 = 1
 EXPORTED_SYMBOLS = (
     "swa_fwd", "swa_bwd", "swa_bwd_preprocess", "swa_bwd_dq", "swa_bwd_dkdv",
     "swa_bwd_workspace_size", "swa_bwd_no_alloc", "swa_check_device",
-    "swa_status_string", "swa_last_cuda_error", "swa_version",
+    "swa_status_string", "swa_last_cuda_error", "swa_version", "swa_lse_row_stride",
 )
 
 
@@ -99,6 +99,8 @@ def _declare(l):
     l.swa_status_string.restype = ctypes.c_char_p
     l.swa_last_cuda_error.argtypes = []
     l.swa_last_cuda_error.restype = ctypes.c_char_p
+    l.swa_lse_row_stride.argtypes = [ctypes.c_int]
+    l.swa_lse_row_stride.restype = ctypes.c_int
     l.swa_version.argtypes = []
     l.swa_version.restype = ctypes.c_int
 

@@ -116,7 +116,7 @@ template <typename T, int D> struct Dkdv {
 };
 
 size_t delta_bytes(const SwaProblem& p) {
-  size_t n = (size_t)p.batch * p.n_q_heads * p.seq_len * sizeof(float);
+  size_t n = (size_t)p.batch * p.n_q_heads * swa::stat_row_stride(p.seq_len) * sizeof(float);
   return (n + 255) & ~(size_t)255;
 }
 
@@ -146,6 +146,7 @@ int build_bwd(const SwaBwdArgs* a, swa::BwdParams* kp) {
   const SwaProblem& p = a->p;
   kp->q = a->q.ptr; kp->k = a->k.ptr; kp->v = a->v.ptr; kp->o = a->o.ptr; kp->dout = a->dout.ptr;
   kp->lse = a->lse;
+  kp->lse_ld = swa::stat_row_stride(p.seq_len);
   kp->delta = static_cast<float*>(a->workspace);
   kp->dq = a->dq.ptr; kp->dk = a->dk.ptr; kp->dv = a->dv.ptr;
   kp->sq = strides(a->q); kp->sk = strides(a->k); kp->sv = strides(a->v); kp->so = strides(a->o);
@@ -166,6 +167,8 @@ int build_bwd(const SwaBwdArgs* a, swa::BwdParams* kp) {
 extern "C" {
 
 int swa_version(void) { return 100; }
+
+int swa_lse_row_stride(int seq_len) { return seq_len < 0 ? 0 : swa::stat_row_stride(seq_len); }
 
 const char* swa_status_string(int s) {
   switch (s) {
@@ -213,6 +216,7 @@ int swa_fwd(const SwaFwdArgs* a, void* stream) {
   if (!a->lse) return SWA_ERR_INVALID_ARG;
   swa::FwdParams kp;
   kp.q = a->q.ptr; kp.k = a->k.ptr; kp.v = a->v.ptr; kp.o = a->o.ptr; kp.lse = a->lse;
+  kp.lse_ld = swa::stat_row_stride(a->p.seq_len);
   kp.sq = strides(a->q); kp.sk = strides(a->k); kp.sv = strides(a->v); kp.so = strides(a->o);
   kp.B = a->p.batch; kp.Hq = a->p.n_q_heads; kp.Hkv = a->p.n_kv_heads; kp.L = a->p.seq_len;
   kp.W = effective_window(a->p.window_size, a->p.seq_len); kp.S = a->p.sink_size;

@@ -22,11 +22,11 @@ __global__ void __launch_bounds__(256) bwd_preprocess_kernel(BwdParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t warp_global = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int64_t row = warp_global * RPW + lane / TPR;
-  const int64_t n_rows = (int64_t)p.B * p.Hq * p.L;
+  const int64_t n_rows = (int64_t)p.B * p.Hq * p.lse_ld;
   float acc = 0.f;
-  if (row < n_rows) {
-    const int i = (int)(row % p.L);
-    const int64_t bh = row / p.L;
+  const int i = (int)(row % p.lse_ld);
+  if (row < n_rows && i < p.L) {
+    const int64_t bh = row / p.lse_ld;
     const int h = (int)(bh % p.Hq), b = (int)(bh / p.Hq);
     const int d0 = (lane % TPR) * 8;
     const uint4 ov = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.o) + b * p.so.b +
@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(128) bwd_dq_mma_kernel(BwdParams p) {
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     int i = r0 + g + r * 8;
-    int64_t idx = ((int64_t)b * p.Hq + h) * L + i;
+    int64_t idx = ((int64_t)b * p.Hq + h) * p.lse_ld + i;
     lse[r] = i < L ? p.lse[idx] : INFINITY;
     dl[r] = i < L ? p.delta[idx] : 0.f;
   }
@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(128) bwd_dq_mma_kernel(BwdParams p) {
 template <typename T, int D>
 cudaError_t launch_bwd_preprocess(const BwdParams& p, cudaStream_t st) {
   constexpr int RPW = 32 / (D / 8);
-  const int64_t n_rows = (int64_t)p.B * p.Hq * p.L;
+  const int64_t n_rows = (int64_t)p.B * p.Hq * p.lse_ld;
   const int64_t rows_per_block = 8 * RPW;
   const int64_t blocks = (n_rows + rows_per_block - 1) / rows_per_block;
   if (blocks == 0) return cudaSuccess;

@@ -33,7 +33,7 @@ namespace swa {
 using namespace sm100;
 
 struct DkdvTmaps {
-  CUtensorMap q, dout, k, v;
+  CUtensorMap q, dout, k, v, lse, delta;
 };
 
 template <int D>
@@ -184,17 +184,12 @@ __global__ void __launch_bounds__(384, 1) bwd_dkdv_tc_kernel(const __grid_consta
           const int h = itm.kvh * G + it / itm.n_qtr;
           const int q0 = (itm.qt_lo + it % itm.n_qtr) * 64;
           unsigned char* Sb = STs + st * C::STAGE;
-          float* lse_s = reinterpret_cast<float*>(Sb + 2 * C::QT_BYTES);
-          const int64_t rb = ((int64_t)itm.b * p.Hq + h) * L;
-#pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            const int i = q0 + k * 32 + lane;
-            lse_s[k * 32 + lane] = i < L ? p.lse[rb + i] : INFINITY;
-            lse_s[64 + k * 32 + lane] = i < L ? p.delta[rb + i] : 0.f;
-          }
-          __syncwarp();
           if (lane == 0) {
-            mbar_arrive_expect_tx(&bar_full[st], 2 * C::QT_BYTES);
+            // LSE / Delta rows are padded to a multiple of 64 (+inf / 0), so q0 is in range
+            const int row = itm.b * p.Hq + h;
+            mbar_arrive_expect_tx(&bar_full[st], 2 * C::QT_BYTES + 512);
+            tma_load_2d(Sb + 2 * C::QT_BYTES, &tm.lse, &bar_full[st], q0, row);
+            tma_load_2d(Sb + 2 * C::QT_BYTES + 256, &tm.delta, &bar_full[st], q0, row);
 #pragma unroll
             for (int c = 0; c < C::NCH; ++c) {
               tma_load_4d(Sb + c * 64 * C::ROWB, &tm.q, &bar_full[st], c * C::CW, q0, h, itm.b);
@@ -460,7 +455,9 @@ cudaError_t launch_bwd_dkdv_tc(const BwdParams& p, cudaStream_t st, int* err) {
   bool ok = make_tmap_bhld(&tm.q, p.q, p.B, p.Hq, p.L, D, p.sq.b, p.sq.h, p.sq.l, C::CW, 64) &&
             make_tmap_bhld(&tm.dout, p.dout, p.B, p.Hq, p.L, D, p.sdo.b, p.sdo.h, p.sdo.l, C::CW, 64) &&
             make_tmap_bhld(&tm.k, p.k, p.B, p.Hkv, p.L, D, p.sk.b, p.sk.h, p.sk.l, C::CW, 128) &&
-            make_tmap_bhld(&tm.v, p.v, p.B, p.Hkv, p.L, D, p.sv.b, p.sv.h, p.sv.l, C::CW, 128);
+            make_tmap_bhld(&tm.v, p.v, p.B, p.Hkv, p.L, D, p.sv.b, p.sv.h, p.sv.l, C::CW, 128) &&
+            make_tmap_rows_f32(&tm.lse, p.lse, (long long)p.B * p.Hq, p.lse_ld, p.lse_ld, 64) &&
+            make_tmap_rows_f32(&tm.delta, p.delta, (long long)p.B * p.Hq, p.lse_ld, p.lse_ld, 64);
   if (!ok) return cudaErrorInvalidValue;
   auto kern = bwd_dkdv_tc_kernel<T, D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);

@@ -13,6 +13,11 @@ namespace swa {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Row stride of the per-row statistics (LSE, Delta): L rounded up to 64, so that every
+// 64-row slice starts 256-byte aligned and can be fetched by TMA; the padding rows hold
+// LSE = +inf and Delta = 0 (they contribute nothing).
+__host__ __device__ inline int stat_row_stride(int L) { return (L + 63) / 64 * 64; }
+
 // ---------------------------------------------------------------------------------------
 // Visibility: key j is seen by query i iff j <= i and (i - j < W or j < S), both < L.
 // Same rule as the reference's masks (flash_attention_gpt_oss.py:80-86, 116-120, 150-155,

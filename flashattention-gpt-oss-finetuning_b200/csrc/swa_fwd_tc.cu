@@ -473,7 +473,10 @@ __global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
           dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
       }
-      if (i < L) p.lse[((int64_t)b * Hq + h) * L + i] = l > 0.f ? rs.m_used + __log2f(l) : -INFINITY;
+      if (i < L)
+        p.lse[((int64_t)b * Hq + h) * p.lse_ld + i] = l > 0.f ? rs.m_used + __log2f(l) : -INFINITY;
+      else if (i < p.lse_ld)
+        p.lse[((int64_t)b * Hq + h) * p.lse_ld + i] = INFINITY;
       if (have_o) {
         tc_fence_before();
         mbar_arrive(&bar_o_free);

@@ -13,11 +13,12 @@ struct FwdParams {
   const void* k;
   const void* v;
   void* o;
-  float* lse;  // [B, Hq, L] contiguous, log2 domain
+  float* lse;  // [B, Hq, lse_ld] rows, log2 domain; rows [L, lse_ld) are set to +inf
   Strides sq, sk, sv, so;
   int B, Hq, Hkv, L, W, S;
   float scale_log2;  // softmax_scale * log2(e)
   int sink_box;      // keys per sink segment (tensor-core forward)
+  int lse_ld;        // row stride of lse (L rounded up to 64)
 };
 
 struct BwdParams {
@@ -26,8 +27,9 @@ struct BwdParams {
   const void* v;
   const void* o;
   const void* dout;
-  const float* lse;  // [B, Hq, L] log2 domain
-  float* delta;      // [B, Hq, L] workspace
+  const float* lse;  // [B, Hq, lse_ld] log2 domain (+inf past L)
+  float* delta;      // [B, Hq, lse_ld] workspace (0 past L)
+  int lse_ld;        // L rounded up to 64
   void* dq;
   void* dk;
   void* dv;

@@ -63,6 +63,22 @@ def _stream(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
 
 
+def lse_row_stride(seq_len: int) -> int:
+    """Row stride of the LSE buffer: seq_len rounded up to 64."""
+    return (seq_len + 63) // 64 * 64
+
+
+def _padded_lse(lse: torch.Tensor, seq_len: int) -> torch.Tensor:
+    """The LSE storage the kernels expect ([B, Hq, lse_row_stride(L)] rows, +inf padding)."""
+    ld = lse_row_stride(seq_len)
+    if lse.dim() == 3 and lse.stride() == (lse.shape[1] * ld, ld, 1) and lse.dtype == torch.float32:
+        return lse
+    full = torch.full((lse.shape[0], lse.shape[1], ld), float("inf"), device=lse.device,
+                      dtype=torch.float32)
+    full[..., :seq_len] = lse[..., :seq_len]
+    return full
+
+
 def _validate(q, k, v, is_causal):
     """The reference's checks (flash_attention_gpt_oss.py:343-354), same exception type."""
     assert is_causal, "Currently, only causal attention is supported"
@@ -83,7 +99,8 @@ def _validate(q, k, v, is_causal):
 def swa_forward(q, k, v, window_size: int, sink_size: int = 0,
                 softmax_scale: Optional[float] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Forward only: returns ``(o, lse)`` where ``lse`` is the base-2 row log-sum-exp
-    ([B, Hq, L] fp32, -inf for a row that sees no key)."""
+    ([B, Hq, L] fp32 view of a buffer whose rows are padded to a multiple of 64; -inf for a
+    row that sees no key).  Pass it unchanged to :func:`swa_backward`."""
     _validate(q, k, v, True)
     d = q.shape[-1]
     if softmax_scale is None:
@@ -92,14 +109,14 @@ def swa_forward(q, k, v, window_size: int, sink_size: int = 0,
     qp, kp, vp = (_prep(t, dk_) for t in (q, k, v))
     b, hq, l, _ = q.shape
     o = torch.empty((b, hq, l, dk_), device=q.device, dtype=q.dtype)
-    lse = torch.empty((b, hq, l), device=q.device, dtype=torch.float32)
+    lse = torch.empty((b, hq, lse_row_stride(l)), device=q.device, dtype=torch.float32)
     args = _lib.SwaFwdArgs(_problem(q, k, window_size, sink_size, softmax_scale, dk_),
                            _tensor(qp), _tensor(kp), _tensor(vp), _tensor(o), lse.data_ptr())
     with torch.cuda.device(q.device):
         _lib.check(_lib.lib().swa_fwd(ctypes.byref(args), _stream(q.device)), "swa_fwd")
     if dk_ != d:
         o = o[..., :d]
-    return o, lse
+    return o, lse[..., :l]
 
 
 def swa_backward(q, k, v, o, lse, do, window_size: int, sink_size: int = 0,
@@ -117,6 +134,7 @@ def swa_backward(q, k, v, o, lse, do, window_size: int, sink_size: int = 0,
     dk = torch.empty((b, k.shape[1], l, dk_), device=q.device, dtype=q.dtype)
     dv = torch.empty_like(dk)
     prob = _problem(q, k, window_size, sink_size, softmax_scale, dk_)
+    lse = _padded_lse(lse, l)
     lib = _lib.lib()
     ws_bytes = lib.swa_bwd_workspace_size(ctypes.byref(prob))
     ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)

@@ -32,7 +32,8 @@ class SwaPlan:
         self.q, self.k, self.v = q, k, v
         self.dout = dout if dout is not None else torch.empty_like(q)
         self.o = torch.empty_like(q)
-        self.lse = torch.empty(q.shape[:3], device=q.device, dtype=torch.float32)
+        b, hq, l = q.shape[:3]
+        self.lse = torch.empty((b, hq, (l + 63) // 64 * 64), device=q.device, dtype=torch.float32)
         self.dq = torch.empty_like(q)
         self.dk = torch.empty_like(k)
         self.dv = torch.empty_like(v)

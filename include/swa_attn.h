@@ -23,9 +23,10 @@
  *   - q, o, dout, dq: [B, Hq, L, D]; k, v, dk, dv: [B, Hkv, L, D]; one dtype for all of
  *     them (fp16 or bf16).  Query head h reads KV head h / (Hq / Hkv).
  *   - Key j is visible to query i iff j <= i and (i - j < window_size or j < sink_size).
- *   - lse: [B, Hq, L] fp32, contiguous.  It is private to this library: it holds the
- *     base-2 log-sum-exp of the scaled scores (log2(e) * ln-LSE), -inf for a row that sees
- *     no key.  (The reference saves the row maximum M instead.)
+ *   - lse: [B, Hq, swa_lse_row_stride(L)] fp32, contiguous (rows padded to a multiple of 64).
+ *     It is private to this library: it holds the base-2 log-sum-exp of the scaled scores
+ *     (log2(e) * ln-LSE), -inf for a row that sees no key, +inf in the padding rows.  (The
+ *     reference saves the row maximum M instead.)
  *   - Every entry point is asynchronous on `stream` (a cudaStream_t, NULL = legacy default
  *     stream), allocates nothing, and returns a SwaStatus.  Work on the device never
  *     waits on another launch.
@@ -81,7 +82,7 @@ typedef struct SwaFwdArgs {
   SwaProblem p;
   SwaTensor q, k, v;  /* inputs  */
   SwaTensor o;        /* output, [B, Hq, L, D] */
-  float* lse;         /* output, [B, Hq, L] contiguous fp32 */
+  float* lse;         /* output, [B, Hq, swa_lse_row_stride(L)] contiguous fp32 */
 } SwaFwdArgs;
 
 typedef struct SwaBwdArgs {
@@ -141,6 +142,9 @@ SWA_API const char* swa_status_string(int status);
 
 /* Text of the last CUDA error seen by a launch on this host thread ("" if none). */
 SWA_API const char* swa_last_cuda_error(void);
+
+/* Row stride (elements) of the lse buffer for sequence length L: L rounded up to 64. */
+SWA_API int swa_lse_row_stride(int seq_len);
 
 /* Version of this library (major*10000 + minor*100 + patch). */
 SWA_API int swa_version(void);
