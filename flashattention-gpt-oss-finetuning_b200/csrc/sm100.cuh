@@ -35,6 +35,10 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
+__device__ __forceinline__ void record_error(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
 // ---------------------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------------------

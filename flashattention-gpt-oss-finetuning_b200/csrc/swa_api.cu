@@ -12,7 +12,7 @@
 namespace swa {
 template <typename T, int D> cudaError_t launch_fwd_tc(const FwdParams&, cudaStream_t, int*);
 template <typename T, int D> cudaError_t launch_bwd_preprocess(const BwdParams&, cudaStream_t);
-template <typename T, int D> cudaError_t launch_bwd_dq_mma(const BwdParams&, cudaStream_t);
+template <typename T, int D> cudaError_t launch_bwd_dq_tc(const BwdParams&, cudaStream_t, int*);
 template <typename T, int D> cudaError_t launch_bwd_dkdv_tc(const BwdParams&, cudaStream_t, int*);
 }  // namespace swa
 
@@ -107,7 +107,9 @@ template <typename T, int D> struct Pre {
   static cudaError_t run(const swa::BwdParams& p, cudaStream_t s) { return swa::launch_bwd_preprocess<T, D>(p, s); }
 };
 template <typename T, int D> struct Dq {
-  static cudaError_t run(const swa::BwdParams& p, cudaStream_t s) { return swa::launch_bwd_dq_mma<T, D>(p, s); }
+  static cudaError_t run(const swa::BwdParams& p, cudaStream_t s) {
+    return swa::launch_bwd_dq_tc<T, D>(p, s, device_error_ptr());
+  }
 };
 template <typename T, int D> struct Dkdv {
   static cudaError_t run(const swa::BwdParams& p, cudaStream_t s) {

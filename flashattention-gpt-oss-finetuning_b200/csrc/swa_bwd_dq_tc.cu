@@ -1,0 +1,383 @@
+// swa_bwd_dq_tc.cu -- dQ kernel on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Persistent kernel.  A work item is one 128-row query tile of one (batch, query head); it
+// walks the same key segments as the forward (sink segments, then 64-key window tiles).
+// Per segment, with Q, dO [128 x D] resident in shared memory for the item and K, V
+// [<=64 keys x D] streamed by TMA:
+//   S  = Q K^T,  dP = dO V^T       (M=128 rows, N=segment keys)        -> TMEM
+//   P  = 2^(S * scale*log2e - LSE_row), masked;  dS = P (dP - Delta_row) -> TMEM, 16-bit
+//        (warps 4..11: each thread owns one query row and 32 key columns)
+//   dQ += dS K                     (A = dS from TMEM, B = K MN-major smem) -> TMEM
+// and dQ * scale is written once per item.  S / dP / dS are double-buffered so the MMAs of
+// segment t+1 overlap the elementwise work on segment t.
+//
+// Reference behaviour followed: the dQ part of _flash_attention_backward_swa_kernel
+// (flash_attention_gpt_oss.py:306-321, 334-338), restricted to the visible key segments
+// (the reference loops over all L keys).  LSE and Delta rows come from the padded
+// [B, Hq, round_up(L, 64)] buffers (+inf / 0 past L), so padded query rows contribute zero.
+//
+// Warp roles (12 warps, 384 threads): warp 0 TMA producer, warp 1 MMA issuer (one thread),
+// warps 4..11 elementwise + epilogue.  Every mbarrier wait is bounded.
+#include <type_traits>
+
+#include "sm100.cuh"
+#include "swa_common.cuh"
+#include "swa_params.cuh"
+#include "tma_host.h"
+
+namespace swa {
+using namespace sm100;
+
+struct DqTmaps {
+  CUtensorMap q, dout, k, v, ks, vs, lse, delta;
+};
+
+template <int D>
+struct DqCfg {
+  static constexpr int BM = 128, BN = 64;
+  static constexpr int CW = D < 64 ? D : 64;
+  static constexpr int NCH = D / CW;
+  static constexpr int ROWB = CW * 2;
+  static constexpr uint32_t SWZ = CW == 64 ? kSw128 : (CW == 32 ? kSw64 : kSw32);
+  static constexpr int QT_BYTES = BM * D * 2;        // Q or dO tile
+  static constexpr int ITEM = 2 * QT_BYTES + 1024;   // Q, dO, LSE[128], Delta[128]
+  static constexpr int NQB = D <= 64 ? 2 : 1;        // item buffers
+  static constexpr int KV_BYTES = BN * D * 2;        // one K or V segment
+  static constexpr int NST = D <= 64 ? 6 : 4;        // K/V stages
+  static constexpr int SMEM = 1024 + NQB * ITEM + NST * 2 * KV_BYTES;
+  static constexpr int S_COL = 0, DP_COL = 128, DS_COL = 256, DQ_COL = 320;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr int THREADS = 384;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(384, 1) bwd_dq_tc_kernel(const __grid_constant__ DqTmaps tm,
+                                                           const BwdParams p, int* err) {
+  using C = DqCfg<D>;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* ITs = smem;                     // [NQB][Q, dO, lse, delta]
+  unsigned char* KVs = smem + C::NQB * C::ITEM;  // [NST][K, V]
+
+  __shared__ uint64_t bar_q_full[C::NQB], bar_q_empty[C::NQB];
+  __shared__ uint64_t bar_full[C::NST], bar_empty[C::NST];
+  __shared__ uint64_t bar_s[2], bar_p[2], bar_acc, bar_acc_free;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_sh;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int L = p.L, W = p.W, S = p.S, Hq = p.Hq;
+  const int G = p.Hq / p.Hkv;
+  const int n_qt = (L + C::BM - 1) / C::BM;
+  const int n_items = p.B * Hq * n_qt;
+  const bool dead = err != nullptr && *reinterpret_cast<volatile int*>(err) != 0;
+
+  if (threadIdx.x == 0) {
+    abort_sh = dead ? 1 : 0;
+    for (int s = 0; s < C::NQB; ++s) {
+      mbar_init(&bar_q_full[s], 1);
+      mbar_init(&bar_q_empty[s], 1);
+    }
+    for (int s = 0; s < C::NST; ++s) {
+      mbar_init(&bar_full[s], 1);
+      mbar_init(&bar_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar_s[s], 1);
+      mbar_init(&bar_p[s], 256);
+    }
+    mbar_init(&bar_acc, 1);
+    mbar_init(&bar_acc_free, 256);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0 && !dead) {
+      tma_prefetch_desc(&tm.q);
+      tma_prefetch_desc(&tm.dout);
+      tma_prefetch_desc(&tm.k);
+      tma_prefetch_desc(&tm.v);
+      int qi = 0, gs = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        int b, h, qt;
+        decode_item(it, Hq, n_qt, &b, &h, &qt);
+        const int q0 = qt * C::BM;
+        const FwdSched sc = fwd_schedule(q0, L, W, S, p.sink_box);
+        const int n = sc.n();
+        if (n == 0) continue;
+        const int kvh = h / G;
+        const int qb = qi % C::NQB;
+        if (qi >= C::NQB && !(ok = mbar_wait(&bar_q_empty[qb], ((qi / C::NQB) - 1) & 1, &abort_sh))) break;
+        unsigned char* Ib = ITs + qb * C::ITEM;
+        const int row = b * Hq + h;
+        mbar_arrive_expect_tx(&bar_q_full[qb], 2 * C::QT_BYTES + 1024);
+#pragma unroll
+        for (int c = 0; c < C::NCH; ++c) {
+          tma_load_4d(Ib + c * C::BM * C::ROWB, &tm.q, &bar_q_full[qb], c * C::CW, q0, h, b);
+          tma_load_4d(Ib + C::QT_BYTES + c * C::BM * C::ROWB, &tm.dout, &bar_q_full[qb], c * C::CW, q0, h, b);
+        }
+        // LSE / Delta rows are padded to a multiple of 64 (+inf / 0)
+        for (int k = 0; k < 2; ++k) {
+          tma_load_2d(Ib + 2 * C::QT_BYTES + k * 256, &tm.lse, &bar_q_full[qb], q0 + 64 * k, row);
+          tma_load_2d(Ib + 2 * C::QT_BYTES + 512 + k * 256, &tm.delta, &bar_q_full[qb], q0 + 64 * k, row);
+        }
+        for (int t = 0; t < n; ++t, ++gs) {
+          const int st = gs % C::NST;
+          if (gs >= C::NST && !(ok = mbar_wait(&bar_empty[st], ((gs / C::NST) - 1) & 1, &abort_sh))) break;
+          int key0, rows;
+          sc.seg(t, &key0, &rows);
+          const bool sink = t < sc.n_sink;
+          unsigned char* Kb = KVs + st * 2 * C::KV_BYTES;
+          mbar_arrive_expect_tx(&bar_full[st], 2 * rows * D * 2);
+#pragma unroll
+          for (int c = 0; c < C::NCH; ++c) {
+            tma_load_4d(Kb + c * rows * C::ROWB, sink ? &tm.ks : &tm.k, &bar_full[st], c * C::CW, key0, kvh, b);
+            tma_load_4d(Kb + C::KV_BYTES + c * rows * C::ROWB, sink ? &tm.vs : &tm.v, &bar_full[st], c * C::CW,
+                        key0, kvh, b);
+          }
+        }
+        ++qi;
+      }
+      if (!ok) {
+        abort_sh = 1;
+        record_error(err, 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0 && !dead) {
+      constexpr uint32_t id_q = idesc_f16(128, D, kBf16, false, true);  // dQ += dS K
+      int qi = 0, gs = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        int b, h, qt;
+        decode_item(it, Hq, n_qt, &b, &h, &qt);
+        const FwdSched sc = fwd_schedule(qt * C::BM, L, W, S, p.sink_box);
+        const int n = sc.n();
+        if (n == 0) continue;
+        const int qb = qi % C::NQB;
+        if (!(ok = mbar_wait(&bar_q_full[qb], (qi / C::NQB) & 1, &abort_sh))) break;
+        const unsigned char* Qb = ITs + qb * C::ITEM;
+        const unsigned char* dOb = Qb + C::QT_BYTES;
+        const int g0 = gs;
+        int next = 0;
+        auto dq_mma = [&](int u) -> bool {
+          const int gu = g0 + u;
+          const int bb = gu & 1;
+          if (!mbar_wait(&bar_p[bb], (gu >> 1) & 1, &abort_sh)) return false;
+          // the previous item's epilogue must have read dQ before it is overwritten
+          if (u == 0 && qi > 0 && !mbar_wait(&bar_acc_free, (qi - 1) & 1, &abort_sh)) return false;
+          tc_fence_after();
+          int key0, rows;
+          sc.seg(u, &key0, &rows);
+          const int st = gu % C::NST;
+          const unsigned char* Kb = KVs + st * 2 * C::KV_BYTES;
+          for (int ks = 0; ks < rows / 16; ++ks) {
+            const uint64_t bk = sdesc(saddr(Kb + ks * 16 * C::ROWB), rows * C::ROWB, 8 * C::ROWB, C::SWZ);
+            mma_ts(tmem + C::DQ_COL, tmem + C::DS_COL + bb * 32 + ks * 8, bk, id_q, (u > 0 || ks > 0) ? 1u : 0u);
+          }
+          mma_commit(&bar_empty[st]);
+          return true;
+        };
+        for (int t = 0; t < n && ok; ++t) {
+          while (ok && next <= t - 2) ok = dq_mma(next++);
+          if (!ok) break;
+          const int gt = g0 + t;
+          const int st = gt % C::NST, bb = gt & 1;
+          if (!(ok = mbar_wait(&bar_full[st], (gt / C::NST) & 1, &abort_sh))) break;
+          tc_fence_after();
+          int key0, rows;
+          sc.seg(t, &key0, &rows);
+          const unsigned char* Kb = KVs + st * 2 * C::KV_BYTES;
+          const unsigned char* Vb = Kb + C::KV_BYTES;
+          const uint32_t id_s = idesc_f16(128, rows, kBf16, false, false);
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks) {
+            const int ch = (ks * 16) / C::CW, within = (ks * 16) % C::CW;
+            const uint64_t aq = sdesc(saddr(Qb + ch * C::BM * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
+            const uint64_t ado = sdesc(saddr(dOb + ch * C::BM * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
+            const uint64_t bk = sdesc(saddr(Kb + ch * rows * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
+            const uint64_t bv = sdesc(saddr(Vb + ch * rows * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
+            mma_ss(tmem + C::S_COL + bb * 64, aq, bk, id_s, ks > 0 ? 1u : 0u);
+            mma_ss(tmem + C::DP_COL + bb * 64, ado, bv, id_s, ks > 0 ? 1u : 0u);
+          }
+          mma_commit(&bar_s[bb]);
+          while (ok && next <= t - 1) ok = dq_mma(next++);
+        }
+        while (ok && next < n) ok = dq_mma(next++);
+        if (!ok) break;
+        mma_commit(&bar_acc);
+        // Q / dO are free, and so are LSE / Delta (read by the elementwise warps before
+        // their first P barrier of the item)
+        mma_commit(&bar_q_empty[qb]);
+        gs += n;
+        ++qi;
+      }
+      if (!ok) {
+        abort_sh = 1;
+        record_error(err, 1);
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ elementwise + epilogue
+    const int quad = warp & 3, half = (warp - 4) >> 2;
+    const int r = quad * 32 + lane;  // query row of the tile (TMEM lane)
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const float sl2 = p.scale_log2;
+    int qi = 0, gs = 0;
+    bool ok = !dead;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+      int b, h, qt;
+      decode_item(it, Hq, n_qt, &b, &h, &qt);
+      const int q0 = qt * C::BM;
+      const int i = q0 + r;
+      const int rw0 = q0 + quad * 32;  // this warp's 32 rows
+      const FwdSched sc = fwd_schedule(q0, L, W, S, p.sink_box);
+      const int n = ok ? sc.n() : 0;
+      float lse_r = 0.f, dl_r = 0.f;
+      if (n > 0) {
+        if (!(ok = mbar_wait(&bar_q_full[qi % C::NQB], (qi / C::NQB) & 1, &abort_sh))) break;
+        const float* st_rows = reinterpret_cast<const float*>(ITs + (qi % C::NQB) * C::ITEM + 2 * C::QT_BYTES);
+        lse_r = st_rows[r];
+        dl_r = st_rows[128 + r];
+      }
+      for (int t = 0; t < n && ok; ++t) {
+        const int gt = gs + t;
+        const int bb = gt & 1;
+        if (!(ok = mbar_wait(&bar_s[bb], (gt >> 1) & 1, &abort_sh))) break;
+        tc_fence_after();
+        int key0, rows;
+        sc.seg(t, &key0, &rows);
+        const int kc0 = key0 + half * 32;  // first key column of this thread
+        const uint32_t tdS = tmem + C::DS_COL + bb * 32 + half * 16 + lane_off;
+        if (half * 32 < rows) {
+          const int kc1 = min(kc0 + 32, key0 + rows);
+          if (block_none_visible(rw0, rw0 + 32, kc0, kc1, W, S, L)) {
+            const uint32_t z[16] = {0u};
+            tmem_st16(tdS, z);
+          } else {
+            const bool full = kc1 == kc0 + 32 && block_all_visible(rw0, rw0 + 32, kc0, kc1, W, S, L);
+            float s[32], dp[32];
+            tmem_ld32(tmem + C::S_COL + bb * 64 + half * 32 + lane_off, reinterpret_cast<uint32_t*>(s));
+            tmem_ld32(tmem + C::DP_COL + bb * 64 + half * 32 + lane_off, reinterpret_cast<uint32_t*>(dp));
+            tmem_ld_wait();
+            // key j = kc0 + c is visible iff c < kc1 - kc0, j <= i and (i - j < W or j < S)
+            const int c_end = kc1 - kc0;
+            const int c_hi = i - kc0;
+            const int c_lo = i - W + 1 - kc0;
+            const int c_sk = S - kc0;
+            uint32_t dw[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              float d2[2];
+#pragma unroll
+              for (int h2 = 0; h2 < 2; ++h2) {
+                const int c = 2 * e + h2;
+                const float pr = fast_exp2(fmaf(s[c], sl2, -lse_r));
+                const float ds = pr * (dp[c] - dl_r);
+                const bool vis = full || (c < c_end && c <= c_hi && (c >= c_lo || c < c_sk));
+                d2[h2] = vis ? ds : 0.f;
+              }
+              dw[e] = Pack<T>::pack(d2[0], d2[1]);
+            }
+            tmem_st16(tdS, dw);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&bar_p[bb]);
+      }
+      // ---- epilogue: dQ * scale, columns [half*D/2, (half+1)*D/2) of row i
+      const bool have = n > 0 && ok;
+      if (have) {
+        ok = mbar_wait(&bar_acc, qi & 1, &abort_sh);
+        tc_fence_after();
+      }
+      T* dqr = static_cast<T*>(p.dq) + b * p.sdq.b + h * p.sdq.h + (int64_t)i * p.sdq.l;
+#pragma unroll
+      for (int c0 = half * (D / 2); c0 < (half + 1) * (D / 2); c0 += 8) {
+        uint32_t a[8];
+        if (have && ok) {
+          asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                       : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]),
+                         "=r"(a[7])
+                       : "r"(tmem + C::DQ_COL + c0 + lane_off));
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) a[e] = 0u;
+        }
+        if (i < L) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            w[e] = Pack<T>::pack(__uint_as_float(a[2 * e]) * p.scale, __uint_as_float(a[2 * e + 1]) * p.scale);
+          *reinterpret_cast<uint4*>(dqr + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      if (have) {
+        tc_fence_before();
+        mbar_arrive(&bar_acc_free);
+        gs += n;
+        ++qi;
+      }
+    }
+    if (!ok && !dead) {
+      abort_sh = 1;
+      record_error(err, 1);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+template <typename T, int D>
+cudaError_t launch_bwd_dq_tc(const BwdParams& p0, cudaStream_t st, int* err) {
+  using C = DqCfg<D>;
+  BwdParams p = p0;
+  const int S = p.S;
+  const int sb = S <= 0 ? 16 : ((S < 64 ? S : 64) + 15) / 16 * 16;
+  p.sink_box = sb;
+  DqTmaps tm;
+  bool ok = make_tmap_bhld(&tm.q, p.q, p.B, p.Hq, p.L, D, p.sq.b, p.sq.h, p.sq.l, C::CW, C::BM) &&
+            make_tmap_bhld(&tm.dout, p.dout, p.B, p.Hq, p.L, D, p.sdo.b, p.sdo.h, p.sdo.l, C::CW, C::BM) &&
+            make_tmap_bhld(&tm.k, p.k, p.B, p.Hkv, p.L, D, p.sk.b, p.sk.h, p.sk.l, C::CW, C::BN) &&
+            make_tmap_bhld(&tm.v, p.v, p.B, p.Hkv, p.L, D, p.sv.b, p.sv.h, p.sv.l, C::CW, C::BN) &&
+            make_tmap_bhld(&tm.ks, p.k, p.B, p.Hkv, p.L, D, p.sk.b, p.sk.h, p.sk.l, C::CW, sb) &&
+            make_tmap_bhld(&tm.vs, p.v, p.B, p.Hkv, p.L, D, p.sv.b, p.sv.h, p.sv.l, C::CW, sb) &&
+            make_tmap_rows_f32(&tm.lse, p.lse, (long long)p.B * p.Hq, p.lse_ld, p.lse_ld, 64) &&
+            make_tmap_rows_f32(&tm.delta, p.delta, (long long)p.B * p.Hq, p.lse_ld, p.lse_ld, 64);
+  if (!ok) return cudaErrorInvalidValue;
+  auto kern = bwd_dq_tc_kernel<T, D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e != cudaSuccess) return e;
+  const int n_items = p.B * p.Hq * ((p.L + C::BM - 1) / C::BM);
+  const int grid = persistent_grid(kern, C::THREADS, C::SMEM, C::TMEM_COLS, n_items);
+  if (grid <= 0) return cudaErrorInvalidConfiguration;
+  kern<<<grid, C::THREADS, C::SMEM, st>>>(tm, p, err);
+  return cudaGetLastError();
+}
+
+#define SWA_INST(T, D) template cudaError_t launch_bwd_dq_tc<T, D>(const BwdParams&, cudaStream_t, int*);
+SWA_INST(__half, 16) SWA_INST(__half, 32) SWA_INST(__half, 64) SWA_INST(__half, 128)
+SWA_INST(__nv_bfloat16, 16) SWA_INST(__nv_bfloat16, 32) SWA_INST(__nv_bfloat16, 64)
+SWA_INST(__nv_bfloat16, 128)
+#undef SWA_INST
+
+}  // namespace swa

@@ -95,9 +95,6 @@ __device__ __forceinline__ DkdvItem dkdv_item(int idx, const BwdParams& p, int G
   return it;
 }
 
-__device__ __forceinline__ void record_err(int* err) {
-  if (err) atomicCAS(err, 0, 1);
-}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(384, 1) bwd_dkdv_tc_kernel(const __grid_constant__ DkdvTmaps tm,
@@ -201,7 +198,7 @@ __global__ void __launch_bounds__(384, 1) bwd_dkdv_tc_kernel(const __grid_consta
       }
       if (!ok) {
         abort_sh = 1;
-        record_err(err);
+        record_error(err, 1);
       }
     }
   } else if (warp == 1) {
@@ -274,7 +271,7 @@ __global__ void __launch_bounds__(384, 1) bwd_dkdv_tc_kernel(const __grid_consta
       }
       if (!ok) {
         abort_sh = 1;
-        record_err(err);
+        record_error(err, 1);
       }
     }
   } else if (warp >= 4) {
@@ -401,7 +398,7 @@ __global__ void __launch_bounds__(384, 1) bwd_dkdv_tc_kernel(const __grid_consta
     }
     if (!ok && !dead) {
       abort_sh = 1;
-      record_err(err);
+      record_error(err, 1);
     }
   }
 

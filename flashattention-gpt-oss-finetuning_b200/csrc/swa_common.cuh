@@ -166,6 +166,54 @@ __host__ __device__ inline long long sink_partial_floats(const SinkSplit& ss, in
 }
 
 // ---------------------------------------------------------------------------------------
+// Key segments of one 128-row query tile (forward and dQ passes): sink segments of `sb` keys
+// (S rounded up to 16, at most 64) below the window, then 64-key window tiles.
+// ---------------------------------------------------------------------------------------
+struct FwdSched {
+  int n_sink, sb, win_lo, n_win;
+  __device__ __forceinline__ int n() const { return n_sink + n_win; }
+  __device__ __forceinline__ void seg(int t, int* key0, int* rows) const {
+    if (t < n_sink) {
+      *key0 = t * sb;
+      *rows = sb;
+    } else {
+      *key0 = (win_lo + t - n_sink) * 64;
+      *rows = 64;
+    }
+  }
+};
+
+__device__ __forceinline__ FwdSched fwd_schedule(int q0, int L, int W, int S, int sb) {
+  FwdSched f;
+  const int q_last = min(q0 + 128, L) - 1;
+  int sink_lim;
+  if (W > 0) {
+    const int lo = max(0, q0 - W + 1);
+    f.win_lo = lo / 64;
+    f.n_win = q_last / 64 - f.win_lo + 1;
+    sink_lim = f.win_lo * 64;
+  } else {
+    f.win_lo = 0;
+    f.n_win = 0;
+    sink_lim = q_last + 1;
+  }
+  const int n_sink_keys = min(min(S, sink_lim), q_last + 1);
+  f.sb = sb;
+  f.n_sink = n_sink_keys > 0 ? (n_sink_keys + sb - 1) / sb : 0;
+  return f;
+}
+
+// Work item = one 128-row query tile of one (batch, query head).  Items are numbered with the
+// query head fastest, so CTAs running at the same time read the same K/V rows (one GQA group)
+// and share them through L2.
+__device__ __forceinline__ void decode_item(int it, int Hq, int n_qt, int* b, int* h, int* qt) {
+  *h = it % Hq;
+  const int rest = it / Hq;
+  *qt = rest % n_qt;
+  *b = rest / n_qt;
+}
+
+// ---------------------------------------------------------------------------------------
 // Element types
 // ---------------------------------------------------------------------------------------
 template <typename T> struct Pack;

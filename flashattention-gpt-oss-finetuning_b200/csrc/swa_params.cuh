@@ -30,6 +30,7 @@ struct BwdParams {
   const float* lse;  // [B, Hq, lse_ld] log2 domain (+inf past L)
   float* delta;      // [B, Hq, lse_ld] workspace (0 past L)
   int lse_ld;        // L rounded up to 64
+  int sink_box;      // keys per sink segment (dQ pass)
   void* dq;
   void* dk;
   void* dv;
