@@ -6,7 +6,7 @@
 // [<=64 keys x D] streamed by TMA:
 //   S  = Q K^T,  dP = dO V^T       (M=128 rows, N=segment keys)        -> TMEM
 //   P  = 2^(S * scale*log2e - LSE_row), masked;  dS = P (dP - Delta_row) -> TMEM, 16-bit
-//        (warps 4..11: each thread owns one query row and 32 key columns)
+//        (warps 4..19: each thread owns one query row and 16 key columns)
 //   dQ += dS K                     (A = dS from TMEM, B = K MN-major smem) -> TMEM
 // and dQ * scale is written once per item.  S / dP / dS are double-buffered so the MMAs of
 // segment t+1 overlap the elementwise work on segment t.
@@ -16,8 +16,10 @@
 // (the reference loops over all L keys).  LSE and Delta rows come from the padded
 // [B, Hq, round_up(L, 64)] buffers (+inf / 0 past L), so padded query rows contribute zero.
 //
-// Warp roles (12 warps, 384 threads): warp 0 TMA producer, warp 1 MMA issuer (one thread),
-// warps 4..11 elementwise + epilogue.  Every mbarrier wait is bounded.
+// Warp roles (20 warps, 640 threads): warp 0 TMA producer, warp 1 MMA issuer (one thread),
+// warps 4..19 elementwise + epilogue: four warps per TMEM lane quadrant, 16 key columns each,
+// so that every scheduler has four independent elementwise warps to hide the TMEM and
+// special-function latencies.  Every mbarrier wait is bounded.
 #include <type_traits>
 
 #include "sm100.cuh"
@@ -47,11 +49,13 @@ struct DqCfg {
   static constexpr int SMEM = 1024 + NQB * ITEM + NST * 2 * KV_BYTES;
   static constexpr int S_COL = 0, DP_COL = 128, DS_COL = 256, DQ_COL = 320;
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr int THREADS = 384;
+  static constexpr int NGRP = 4;            // elementwise column groups
+  static constexpr int CPG = 64 / NGRP;      // key columns per group
+  static constexpr int THREADS = 128 + 128 * NGRP;
 };
 
 template <typename T, int D>
-__global__ void __launch_bounds__(384, 1) bwd_dq_tc_kernel(const __grid_constant__ DqTmaps tm,
+__global__ void __launch_bounds__(640, 1) bwd_dq_tc_kernel(const __grid_constant__ DqTmaps tm,
                                                            const BwdParams p, int* err) {
   using C = DqCfg<D>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -86,10 +90,10 @@ __global__ void __launch_bounds__(384, 1) bwd_dq_tc_kernel(const __grid_constant
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bar_s[s], 1);
-      mbar_init(&bar_p[s], 256);
+      mbar_init(&bar_p[s], 128 * C::NGRP);
     }
     mbar_init(&bar_acc, 1);
-    mbar_init(&bar_acc_free, 256);
+    mbar_init(&bar_acc_free, 128 * C::NGRP);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -232,7 +236,8 @@ __global__ void __launch_bounds__(384, 1) bwd_dq_tc_kernel(const __grid_constant
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ elementwise + epilogue
-    const int quad = warp & 3, half = (warp - 4) >> 2;
+    const int quad = warp & 3, grp = (warp - 4) >> 2;
+    constexpr int CPG = C::CPG;
     const int r = quad * 32 + lane;  // query row of the tile (TMEM lane)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float sl2 = p.scale_log2;
@@ -260,27 +265,27 @@ __global__ void __launch_bounds__(384, 1) bwd_dq_tc_kernel(const __grid_constant
         tc_fence_after();
         int key0, rows;
         sc.seg(t, &key0, &rows);
-        const int kc0 = key0 + half * 32;  // first key column of this thread
-        const uint32_t tdS = tmem + C::DS_COL + bb * 32 + half * 16 + lane_off;
-        if (half * 32 < rows) {
-          const int kc1 = min(kc0 + 32, key0 + rows);
+        const int kc0 = key0 + grp * CPG;  // first key column of this thread
+        const uint32_t tdS = tmem + C::DS_COL + bb * 32 + grp * (CPG / 2) + lane_off;
+        if (grp * CPG < rows) {
+          const int kc1 = min(kc0 + CPG, key0 + rows);
           if (block_none_visible(rw0, rw0 + 32, kc0, kc1, W, S, L)) {
-            const uint32_t z[16] = {0u};
-            tmem_st16(tdS, z);
+            const uint32_t z[8] = {0u};
+            tmem_st8(tdS, z);
           } else {
-            const bool full = kc1 == kc0 + 32 && block_all_visible(rw0, rw0 + 32, kc0, kc1, W, S, L);
-            float s[32], dp[32];
-            tmem_ld32(tmem + C::S_COL + bb * 64 + half * 32 + lane_off, reinterpret_cast<uint32_t*>(s));
-            tmem_ld32(tmem + C::DP_COL + bb * 64 + half * 32 + lane_off, reinterpret_cast<uint32_t*>(dp));
+            const bool full = kc1 == kc0 + CPG && block_all_visible(rw0, rw0 + 32, kc0, kc1, W, S, L);
+            float s[CPG], dp[CPG];
+            tmem_ld16(tmem + C::S_COL + bb * 64 + grp * CPG + lane_off, reinterpret_cast<uint32_t*>(s));
+            tmem_ld16(tmem + C::DP_COL + bb * 64 + grp * CPG + lane_off, reinterpret_cast<uint32_t*>(dp));
             tmem_ld_wait();
             // key j = kc0 + c is visible iff c < kc1 - kc0, j <= i and (i - j < W or j < S)
             const int c_end = kc1 - kc0;
             const int c_hi = i - kc0;
             const int c_lo = i - W + 1 - kc0;
             const int c_sk = S - kc0;
-            uint32_t dw[16];
+            uint32_t dw[CPG / 2];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
+            for (int e = 0; e < CPG / 2; ++e) {
               float d2[2];
 #pragma unroll
               for (int h2 = 0; h2 < 2; ++h2) {
@@ -292,14 +297,14 @@ __global__ void __launch_bounds__(384, 1) bwd_dq_tc_kernel(const __grid_constant
               }
               dw[e] = Pack<T>::pack(d2[0], d2[1]);
             }
-            tmem_st16(tdS, dw);
+            tmem_st8(tdS, dw);
           }
         }
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&bar_p[bb]);
       }
-      // ---- epilogue: dQ * scale, columns [half*D/2, (half+1)*D/2) of row i
+      // ---- epilogue: dQ * scale of row i, 8-column chunks dealt round-robin to the groups
       const bool have = n > 0 && ok;
       if (have) {
         ok = mbar_wait(&bar_acc, qi & 1, &abort_sh);
@@ -307,7 +312,7 @@ __global__ void __launch_bounds__(384, 1) bwd_dq_tc_kernel(const __grid_constant
       }
       T* dqr = static_cast<T*>(p.dq) + b * p.sdq.b + h * p.sdq.h + (int64_t)i * p.sdq.l;
 #pragma unroll
-      for (int c0 = half * (D / 2); c0 < (half + 1) * (D / 2); c0 += 8) {
+      for (int c0 = grp * 8; c0 < D; c0 += 8 * C::NGRP) {
         uint32_t a[8];
         if (have && ok) {
           asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"

@@ -13,14 +13,16 @@
 //   S^T  = K Q^T      (M=128 keys, N=64 rows)  -> TMEM   (tcgen05.mma, A and B K-major smem)
 //   dP^T = V dO^T                               -> TMEM
 //   P^T  = 2^(S^T * scale*log2e - LSE_row), masked;  dS^T = P^T (dP^T - Delta_row)
-//          (warps 4..11; each thread owns one key row and 32 query columns)  -> TMEM, 16-bit
+//          (warps 4..19; each thread owns one key row and 16 query columns)  -> TMEM, 16-bit
 //   dV  += P^T dO     (A = P^T from TMEM, B = dO MN-major smem)
 //   dK  += dS^T Q     (A = dS^T from TMEM, B = Q MN-major smem)
 // S^T / dP^T / P^T / dS^T are double-buffered (head dims <= 64) so the MMAs of step t+1 run
 // while the elementwise warps work on step t.
 //
-// Warp roles (12 warps, 384 threads): warp 0 TMA producer (K/V per item, Q/dO + LSE/Delta per
-// step), warp 1 MMA issuer (one thread), warps 4..11 elementwise + epilogue.
+// Warp roles (20 warps, 640 threads): warp 0 TMA producer (K/V per item, Q/dO + LSE/Delta per
+// step), warp 1 MMA issuer (one thread), warps 4..19 elementwise + epilogue: four warps per
+// TMEM lane quadrant, 16 query columns each (no row reductions are needed in the backward,
+// so the split costs nothing and gives every scheduler four independent warps).
 // Every mbarrier wait is bounded; a wait that gives up records an error and the CTA exits.
 #include <type_traits>
 
@@ -53,7 +55,9 @@ struct DkdvCfg {
   static constexpr int S_COL = 0, DP_COL = 64 * NB, P_COL = 128 * NB, DS_COL = 160 * NB;
   static constexpr int DK_COL = 192 * NB, DV_COL = 192 * NB + D;
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr int THREADS = 384;
+  static constexpr int NGRP = 4;        // elementwise column groups
+  static constexpr int CPG = 64 / NGRP;  // query columns per group
+  static constexpr int THREADS = 128 + 128 * NGRP;
 };
 
 struct DkdvItem {
@@ -97,7 +101,7 @@ __device__ __forceinline__ DkdvItem dkdv_item(int idx, const BwdParams& p, int G
 
 
 template <typename T, int D>
-__global__ void __launch_bounds__(384, 1) bwd_dkdv_tc_kernel(const __grid_constant__ DkdvTmaps tm,
+__global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_constant__ DkdvTmaps tm,
                                                              const BwdParams p, int* err) {
   using C = DkdvCfg<D>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -133,10 +137,10 @@ __global__ void __launch_bounds__(384, 1) bwd_dkdv_tc_kernel(const __grid_consta
     }
     for (int s = 0; s < C::NB; ++s) {
       mbar_init(&bar_s[s], 1);
-      mbar_init(&bar_p[s], 256);
+      mbar_init(&bar_p[s], 128 * C::NGRP);
     }
     mbar_init(&bar_acc, 1);
-    mbar_init(&bar_acc_free, 256);
+    mbar_init(&bar_acc_free, 128 * C::NGRP);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -276,7 +280,8 @@ __global__ void __launch_bounds__(384, 1) bwd_dkdv_tc_kernel(const __grid_consta
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ elementwise + epilogue
-    const int quad = warp & 3, half = (warp - 4) >> 2;
+    const int quad = warp & 3, grp = (warp - 4) >> 2;
+    constexpr int CPG = C::CPG;
     const int r = quad * 32 + lane;  // key row of the tile (TMEM lane)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float sl2 = p.scale_log2;
@@ -294,27 +299,27 @@ __global__ void __launch_bounds__(384, 1) bwd_dkdv_tc_kernel(const __grid_consta
         if (!(ok = mbar_wait(&bar_s[bb], (gt / C::NB) & 1, &abort_sh))) break;
         tc_fence_after();
         const int it = itm.it0 + t;
-        const int qc0 = (itm.qt_lo + it % itm.n_qtr) * 64 + half * 32;  // first query column
-        const uint32_t tP = tmem + C::P_COL + bb * 32 + half * 16 + lane_off;
-        const uint32_t tdS = tmem + C::DS_COL + bb * 32 + half * 16 + lane_off;
-        if (block_none_visible(qc0, qc0 + 32, kw0, kw0 + 32, W, S, L)) {
-          const uint32_t z[16] = {0u};
-          tmem_st16(tP, z);
-          tmem_st16(tdS, z);
+        const int qc0 = (itm.qt_lo + it % itm.n_qtr) * 64 + grp * CPG;  // first query column
+        const uint32_t tP = tmem + C::P_COL + bb * 32 + grp * (CPG / 2) + lane_off;
+        const uint32_t tdS = tmem + C::DS_COL + bb * 32 + grp * (CPG / 2) + lane_off;
+        if (block_none_visible(qc0, qc0 + CPG, kw0, kw0 + 32, W, S, L)) {
+          const uint32_t z[8] = {0u};
+          tmem_st8(tP, z);
+          tmem_st8(tdS, z);
         } else {
-          const bool full = block_all_visible(qc0, qc0 + 32, kw0, kw0 + 32, W, S, L);
-          float s[32], dp[32];
-          tmem_ld32(tmem + C::S_COL + bb * 64 + half * 32 + lane_off, reinterpret_cast<uint32_t*>(s));
-          tmem_ld32(tmem + C::DP_COL + bb * 64 + half * 32 + lane_off, reinterpret_cast<uint32_t*>(dp));
-          const float* lse_s = reinterpret_cast<const float*>(STs + st * C::STAGE + 2 * C::QT_BYTES) + half * 32;
+          const bool full = block_all_visible(qc0, qc0 + CPG, kw0, kw0 + 32, W, S, L);
+          float s[CPG], dp[CPG];
+          tmem_ld16(tmem + C::S_COL + bb * 64 + grp * CPG + lane_off, reinterpret_cast<uint32_t*>(s));
+          tmem_ld16(tmem + C::DP_COL + bb * 64 + grp * CPG + lane_off, reinterpret_cast<uint32_t*>(dp));
+          const float* lse_s = reinterpret_cast<const float*>(STs + st * C::STAGE + 2 * C::QT_BYTES) + grp * CPG;
           const float* dl_s = lse_s + 64;
           tmem_ld_wait();
           // query i = qc0 + c sees key j iff c >= c_min and (c < c_max or j < S)
           const int c_min = j - qc0;
           const int c_max = (W > 0 && j >= S) ? j + W - qc0 : (j < S ? 1 << 30 : -(1 << 30));
-          uint32_t pw[16], dw[16];
+          uint32_t pw[CPG / 2], dw[CPG / 2];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
+          for (int e = 0; e < CPG / 2; ++e) {
             float pv[2], dv[2];
 #pragma unroll
             for (int h2 = 0; h2 < 2; ++h2) {
@@ -327,14 +332,14 @@ __global__ void __launch_bounds__(384, 1) bwd_dkdv_tc_kernel(const __grid_consta
             pw[e] = Pack<T>::pack(pv[0], pv[1]);
             dw[e] = Pack<T>::pack(dv[0], dv[1]);
           }
-          tmem_st16(tP, pw);
-          tmem_st16(tdS, dw);
+          tmem_st8(tP, pw);
+          tmem_st8(tdS, dw);
         }
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&bar_p[bb]);
       }
-      // ---- epilogue: this thread writes columns [half*D/2, (half+1)*D/2) of key row j
+      // ---- epilogue: key row j, 8-column chunks dealt round-robin to the column groups
       const bool have = itm.n > 0 && ok;
       if (have) {
         ok = mbar_wait(&bar_acc, qi & 1, &abort_sh);
@@ -351,7 +356,7 @@ __global__ void __launch_bounds__(384, 1) bwd_dkdv_tc_kernel(const __grid_consta
       T* dkr = static_cast<T*>(p.dk) + itm.b * p.sdk.b + itm.kvh * p.sdk.h + (int64_t)j * p.sdk.l;
       T* dvr = static_cast<T*>(p.dv) + itm.b * p.sdv.b + itm.kvh * p.sdv.h + (int64_t)j * p.sdv.l;
 #pragma unroll
-      for (int c0 = half * (D / 2); c0 < (half + 1) * (D / 2); c0 += 8) {
+      for (int c0 = grp * 8; c0 < D; c0 += 8 * C::NGRP) {
         uint32_t ka[8], va[8];
         if (have && ok) {
           // 32x32b.x8 loads (8 columns) keep the loop uniform for every head dim
