@@ -43,19 +43,27 @@ struct DqCfg {
   static constexpr uint32_t SWZ = CW == 64 ? kSw128 : (CW == 32 ? kSw64 : kSw32);
   static constexpr int QT_BYTES = BM * D * 2;        // Q or dO tile
   static constexpr int ITEM = 2 * QT_BYTES + 1024;   // Q, dO, LSE[128], Delta[128]
+#ifndef SWA_DQ_NB
+#define SWA_DQ_NB 2
+#endif
+#ifndef SWA_DQ_NGRP
+#define SWA_DQ_NGRP 4
+#endif
+  static constexpr int NB = D <= 64 ? SWA_DQ_NB : 1;  // TMEM buffers of S, dP, dS
   static constexpr int NQB = D <= 64 ? 2 : 1;        // item buffers
   static constexpr int KV_BYTES = BN * D * 2;        // one K or V segment
   static constexpr int NST = D <= 64 ? 6 : 4;        // K/V stages
   static constexpr int SMEM = 1024 + NQB * ITEM + NST * 2 * KV_BYTES;
-  static constexpr int S_COL = 0, DP_COL = 128, DS_COL = 256, DQ_COL = 320;
-  static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr int NGRP = 4;            // elementwise column groups
+  static constexpr int S_COL = 0, DP_COL = 64 * NB, DS_COL = 128 * NB, DQ_COL = 160 * NB;
+  static constexpr uint32_t TMEM_COLS = (160 * NB + D) <= 256 ? 256 : 512;
+  static constexpr int CTAS = TMEM_COLS == 256 ? 2 : 1;  // resident CTAs per SM
+  static constexpr int NGRP = SWA_DQ_NGRP;  // elementwise column groups
   static constexpr int CPG = 64 / NGRP;      // key columns per group
   static constexpr int THREADS = 128 + 128 * NGRP;
 };
 
 template <typename T, int D>
-__global__ void __launch_bounds__(640, 1) bwd_dq_tc_kernel(const __grid_constant__ DqTmaps tm,
+__global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, (D <= 64 && SWA_DQ_NB == 1) ? 2 : 1) bwd_dq_tc_kernel(const __grid_constant__ DqTmaps tm,
                                                            const BwdParams p, int* err) {
   using C = DqCfg<D>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -67,7 +75,7 @@ __global__ void __launch_bounds__(640, 1) bwd_dq_tc_kernel(const __grid_constant
 
   __shared__ uint64_t bar_q_full[C::NQB], bar_q_empty[C::NQB];
   __shared__ uint64_t bar_full[C::NST], bar_empty[C::NST];
-  __shared__ uint64_t bar_s[2], bar_p[2], bar_acc, bar_acc_free;
+  __shared__ uint64_t bar_s[C::NB], bar_p[C::NB], bar_acc, bar_acc_free;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
 
@@ -88,7 +96,7 @@ __global__ void __launch_bounds__(640, 1) bwd_dq_tc_kernel(const __grid_constant
       mbar_init(&bar_full[s], 1);
       mbar_init(&bar_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < C::NB; ++s) {
       mbar_init(&bar_s[s], 1);
       mbar_init(&bar_p[s], 128 * C::NGRP);
     }
@@ -179,8 +187,8 @@ __global__ void __launch_bounds__(640, 1) bwd_dq_tc_kernel(const __grid_constant
         int next = 0;
         auto dq_mma = [&](int u) -> bool {
           const int gu = g0 + u;
-          const int bb = gu & 1;
-          if (!mbar_wait(&bar_p[bb], (gu >> 1) & 1, &abort_sh)) return false;
+          const int bb = gu % C::NB;
+          if (!mbar_wait(&bar_p[bb], (gu / C::NB) & 1, &abort_sh)) return false;
           // the previous item's epilogue must have read dQ before it is overwritten
           if (u == 0 && qi > 0 && !mbar_wait(&bar_acc_free, (qi - 1) & 1, &abort_sh)) return false;
           tc_fence_after();
@@ -196,10 +204,10 @@ __global__ void __launch_bounds__(640, 1) bwd_dq_tc_kernel(const __grid_constant
           return true;
         };
         for (int t = 0; t < n && ok; ++t) {
-          while (ok && next <= t - 2) ok = dq_mma(next++);
+          while (ok && next <= t - C::NB) ok = dq_mma(next++);
           if (!ok) break;
           const int gt = g0 + t;
-          const int st = gt % C::NST, bb = gt & 1;
+          const int st = gt % C::NST, bb = gt % C::NB;
           if (!(ok = mbar_wait(&bar_full[st], (gt / C::NST) & 1, &abort_sh))) break;
           tc_fence_after();
           int key0, rows;
@@ -260,44 +268,48 @@ __global__ void __launch_bounds__(640, 1) bwd_dq_tc_kernel(const __grid_constant
       }
       for (int t = 0; t < n && ok; ++t) {
         const int gt = gs + t;
-        const int bb = gt & 1;
-        if (!(ok = mbar_wait(&bar_s[bb], (gt >> 1) & 1, &abort_sh))) break;
+        const int bb = gt % C::NB;
+        if (!(ok = mbar_wait(&bar_s[bb], (gt / C::NB) & 1, &abort_sh))) break;
         tc_fence_after();
         int key0, rows;
         sc.seg(t, &key0, &rows);
-        const int kc0 = key0 + grp * CPG;  // first key column of this thread
-        const uint32_t tdS = tmem + C::DS_COL + bb * 32 + grp * (CPG / 2) + lane_off;
-        if (grp * CPG < rows) {
-          const int kc1 = min(kc0 + CPG, key0 + rows);
-          if (block_none_visible(rw0, rw0 + 32, kc0, kc1, W, S, L)) {
-            const uint32_t z[8] = {0u};
-            tmem_st8(tdS, z);
-          } else {
-            const bool full = kc1 == kc0 + CPG && block_all_visible(rw0, rw0 + 32, kc0, kc1, W, S, L);
-            float s[CPG], dp[CPG];
-            tmem_ld16(tmem + C::S_COL + bb * 64 + grp * CPG + lane_off, reinterpret_cast<uint32_t*>(s));
-            tmem_ld16(tmem + C::DP_COL + bb * 64 + grp * CPG + lane_off, reinterpret_cast<uint32_t*>(dp));
-            tmem_ld_wait();
-            // key j = kc0 + c is visible iff c < kc1 - kc0, j <= i and (i - j < W or j < S)
-            const int c_end = kc1 - kc0;
-            const int c_hi = i - kc0;
-            const int c_lo = i - W + 1 - kc0;
-            const int c_sk = S - kc0;
-            uint32_t dw[CPG / 2];
 #pragma unroll
-            for (int e = 0; e < CPG / 2; ++e) {
-              float d2[2];
+        for (int ch = 0; ch < CPG / 16; ++ch) {
+          const int col = grp * CPG + ch * 16;  // first of this chunk's 16 key columns
+          const int kc0 = key0 + col;
+          const uint32_t tdS = tmem + C::DS_COL + bb * 32 + col / 2 + lane_off;
+          if (col < rows) {
+            const int kc1 = min(kc0 + 16, key0 + rows);
+            if (block_none_visible(rw0, rw0 + 32, kc0, kc1, W, S, L)) {
+              const uint32_t z[8] = {0u};
+              tmem_st8(tdS, z);
+            } else {
+              const bool full = kc1 == kc0 + 16 && block_all_visible(rw0, rw0 + 32, kc0, kc1, W, S, L);
+              float s[16], dp[16];
+              tmem_ld16(tmem + C::S_COL + bb * 64 + col + lane_off, reinterpret_cast<uint32_t*>(s));
+              tmem_ld16(tmem + C::DP_COL + bb * 64 + col + lane_off, reinterpret_cast<uint32_t*>(dp));
+              tmem_ld_wait();
+              // key j = kc0 + c is visible iff c < kc1 - kc0, j <= i and (i - j < W or j < S)
+              const int c_end = kc1 - kc0;
+              const int c_hi = i - kc0;
+              const int c_lo = i - W + 1 - kc0;
+              const int c_sk = S - kc0;
+              uint32_t dw[8];
 #pragma unroll
-              for (int h2 = 0; h2 < 2; ++h2) {
-                const int c = 2 * e + h2;
-                const float pr = fast_exp2(fmaf(s[c], sl2, -lse_r));
-                const float ds = pr * (dp[c] - dl_r);
-                const bool vis = full || (c < c_end && c <= c_hi && (c >= c_lo || c < c_sk));
-                d2[h2] = vis ? ds : 0.f;
+              for (int e = 0; e < 8; ++e) {
+                float d2[2];
+#pragma unroll
+                for (int h2 = 0; h2 < 2; ++h2) {
+                  const int c = 2 * e + h2;
+                  const float pr = fast_exp2(fmaf(s[c], sl2, -lse_r));
+                  const float ds = pr * (dp[c] - dl_r);
+                  const bool vis = full || (c < c_end && c <= c_hi && (c >= c_lo || c < c_sk));
+                  d2[h2] = vis ? ds : 0.f;
+                }
+                dw[e] = Pack<T>::pack(d2[0], d2[1]);
               }
-              dw[e] = Pack<T>::pack(d2[0], d2[1]);
+              tmem_st8(tdS, dw);
             }
-            tmem_st8(tdS, dw);
           }
         }
         tmem_st_wait();
