@@ -8,8 +8,10 @@
 //   P  = 2^(S * scale*log2e - LSE_row), masked;  dS = P (dP - Delta_row) -> TMEM, 16-bit
 //        (warps 4..19: each thread owns one query row and 16 key columns)
 //   dQ += dS K                     (A = dS from TMEM, B = K MN-major smem) -> TMEM
-// and dQ * scale is written once per item.  S / dP / dS are double-buffered so the MMAs of
-// segment t+1 overlap the elementwise work on segment t.
+// and dQ * scale is written once per item.  S and dP have NB = 3 TMEM buffers (2 for
+// D = 128) and dS is written back over the S columns each warp has read; the dQ MMAs of a
+// segment are issued just before its buffer is reused, so S runs ahead of the elementwise
+// warps.
 //
 // Reference behaviour followed: the dQ part of _flash_attention_backward_swa_kernel
 // (flash_attention_gpt_oss.py:306-321, 334-338), restricted to the visible key segments
@@ -44,26 +46,27 @@ struct DqCfg {
   static constexpr int QT_BYTES = BM * D * 2;        // Q or dO tile
   static constexpr int ITEM = 2 * QT_BYTES + 1024;   // Q, dO, LSE[128], Delta[128]
 #ifndef SWA_DQ_NB
-#define SWA_DQ_NB 2
+#define SWA_DQ_NB 3
 #endif
 #ifndef SWA_DQ_NGRP
 #define SWA_DQ_NGRP 4
 #endif
-  static constexpr int NB = D <= 64 ? SWA_DQ_NB : 1;  // TMEM buffers of S, dP, dS
+  static constexpr int NB = D <= 64 ? SWA_DQ_NB : 2;  // TMEM buffers of S (and dS) and dP
   static constexpr int NQB = D <= 64 ? 2 : 1;        // item buffers
   static constexpr int KV_BYTES = BN * D * 2;        // one K or V segment
-  static constexpr int NST = D <= 64 ? 6 : 4;        // K/V stages
+  static constexpr int NST = D <= 64 ? 8 : 4;        // K/V stages
   static constexpr int SMEM = 1024 + NQB * ITEM + NST * 2 * KV_BYTES;
-  static constexpr int S_COL = 0, DP_COL = 64 * NB, DS_COL = 128 * NB, DQ_COL = 160 * NB;
-  static constexpr uint32_t TMEM_COLS = (160 * NB + D) <= 256 ? 256 : 512;
-  static constexpr int CTAS = TMEM_COLS == 256 ? 2 : 1;  // resident CTAs per SM
+  // dS of a segment overwrites its S columns: key columns [16k, 16k+16) of S hold, after the
+  // elementwise pass, dS keys 16k..16k+15 in [16k, 16k+8) (the A operand of MMA K-step k).
+  static constexpr int S_COL = 0, DP_COL = 64 * NB, DQ_COL = 128 * NB;
+  static constexpr uint32_t TMEM_COLS = (128 * NB + D) <= 256 ? 256 : 512;
   static constexpr int NGRP = SWA_DQ_NGRP;  // elementwise column groups
   static constexpr int CPG = 64 / NGRP;      // key columns per group
   static constexpr int THREADS = 128 + 128 * NGRP;
 };
 
 template <typename T, int D>
-__global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, (D <= 64 && SWA_DQ_NB == 1) ? 2 : 1) bwd_dq_tc_kernel(const __grid_constant__ DqTmaps tm,
+__global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(const __grid_constant__ DqTmaps tm,
                                                            const BwdParams p, int* err) {
   using C = DqCfg<D>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -198,7 +201,7 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, (D <= 64 && SWA_DQ_NB
           const unsigned char* Kb = KVs + st * 2 * C::KV_BYTES;
           for (int ks = 0; ks < rows / 16; ++ks) {
             const uint64_t bk = sdesc(saddr(Kb + ks * 16 * C::ROWB), rows * C::ROWB, 8 * C::ROWB, C::SWZ);
-            mma_ts(tmem + C::DQ_COL, tmem + C::DS_COL + bb * 32 + ks * 8, bk, id_q, (u > 0 || ks > 0) ? 1u : 0u);
+            mma_ts(tmem + C::DQ_COL, tmem + C::S_COL + bb * 64 + ks * 16, bk, id_q, (u > 0 || ks > 0) ? 1u : 0u);
           }
           mma_commit(&bar_empty[st]);
           return true;
@@ -226,7 +229,6 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, (D <= 64 && SWA_DQ_NB
             mma_ss(tmem + C::DP_COL + bb * 64, ado, bv, id_s, ks > 0 ? 1u : 0u);
           }
           mma_commit(&bar_s[bb]);
-          while (ok && next <= t - 1) ok = dq_mma(next++);
         }
         while (ok && next < n) ok = dq_mma(next++);
         if (!ok) break;
@@ -277,7 +279,7 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, (D <= 64 && SWA_DQ_NB
         for (int ch = 0; ch < CPG / 16; ++ch) {
           const int col = grp * CPG + ch * 16;  // first of this chunk's 16 key columns
           const int kc0 = key0 + col;
-          const uint32_t tdS = tmem + C::DS_COL + bb * 32 + col / 2 + lane_off;
+          const uint32_t tdS = tmem + C::S_COL + bb * 64 + col + lane_off;  // over this chunk's S
           if (col < rows) {
             const int kc1 = min(kc0 + 16, key0 + rows);
             if (block_none_visible(rw0, rw0 + 32, kc0, kc1, W, S, L)) {

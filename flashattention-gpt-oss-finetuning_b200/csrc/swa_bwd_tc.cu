@@ -16,8 +16,10 @@
 //          (warps 4..19; each thread owns one key row and 16 query columns)  -> TMEM, 16-bit
 //   dV  += P^T dO     (A = P^T from TMEM, B = dO MN-major smem)
 //   dK  += dS^T Q     (A = dS^T from TMEM, B = Q MN-major smem)
-// S^T / dP^T / P^T / dS^T are double-buffered (head dims <= 64) so the MMAs of step t+1 run
-// while the elementwise warps work on step t.
+// S^T and dP^T have NB = 3 TMEM buffers (2 for D = 128); P^T and dS^T are written back over
+// the S^T columns each elementwise warp has read.  The MMA thread issues S^T / dP^T of step t
+// as soon as step t - NB's buffer is released and the dV / dK MMAs of a step only just
+// before its buffer is reused, so S^T runs up to NB - 1 steps ahead of the elementwise warps.
 //
 // Warp roles (20 warps, 640 threads): warp 0 TMA producer (K/V per item, Q/dO + LSE/Delta per
 // step), warp 1 MMA issuer (one thread), warps 4..19 elementwise + epilogue: four warps per
@@ -49,11 +51,14 @@ struct DkdvCfg {
   static constexpr int QT_BYTES = BM * D * 2;
   static constexpr int STAGE = 2 * QT_BYTES + 1024;  // Q, dO, then LSE[64], Delta[64]
   static constexpr int NKV = D <= 64 ? 2 : 1;        // K/V buffers (items in flight)
-  static constexpr int NST = D <= 64 ? 4 : 3;        // Q/dO stages
-  static constexpr int NB = D <= 64 ? 2 : 1;         // TMEM buffers of S^T, dP^T, P^T, dS^T
+  static constexpr int NST = D <= 64 ? 6 : 4;        // Q/dO stages
+  static constexpr int NB = D <= 64 ? 3 : 2;         // TMEM buffers of S^T (P^T, dS^T) and dP^T
   static constexpr int SMEM = 1024 + NKV * 2 * KV_BYTES + NST * STAGE;
-  static constexpr int S_COL = 0, DP_COL = 64 * NB, P_COL = 128 * NB, DS_COL = 160 * NB;
-  static constexpr int DK_COL = 192 * NB, DV_COL = 192 * NB + D;
+  // P^T and dS^T of a step overwrite its S^T columns: query columns [16k, 16k+16) of S^T
+  // hold, after the elementwise pass, P^T in [16k, 16k+8) and dS^T in [16k+8, 16k+16)
+  // (two 16-bit values per column), the A operand of MMA K-step k.
+  static constexpr int S_COL = 0, DP_COL = 64 * NB;
+  static constexpr int DK_COL = 128 * NB, DV_COL = 128 * NB + D;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr int NGRP = 4;        // elementwise column groups
   static constexpr int CPG = 64 / NGRP;  // query columns per group
@@ -231,20 +236,20 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
           const int st = gu % C::NST;
           const unsigned char* Qb = STs + st * C::STAGE;
           const unsigned char* dOb = Qb + C::QT_BYTES;
-          const uint32_t tP = tmem + C::P_COL + bb * 32, tdS = tmem + C::DS_COL + bb * 32;
+          const uint32_t tS = tmem + C::S_COL + bb * 64;
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {  // K = 64 query rows, 16 per MMA
             const uint64_t bdo = sdesc(saddr(dOb + ks * 16 * C::ROWB), 64 * C::ROWB, 8 * C::ROWB, C::SWZ);
             const uint64_t bq = sdesc(saddr(Qb + ks * 16 * C::ROWB), 64 * C::ROWB, 8 * C::ROWB, C::SWZ);
             const uint32_t acc = (u > 0 || ks > 0) ? 1u : 0u;
-            mma_ts(tmem + C::DV_COL, tP + ks * 8, bdo, id_a, acc);
-            mma_ts(tmem + C::DK_COL, tdS + ks * 8, bq, id_a, acc);
+            mma_ts(tmem + C::DV_COL, tS + ks * 16, bdo, id_a, acc);
+            mma_ts(tmem + C::DK_COL, tS + ks * 16 + 8, bq, id_a, acc);
           }
           mma_commit(&bar_empty[st]);
           return true;
         };
         for (int t = 0; t < itm.n && ok; ++t) {
-          // free the TMEM buffer that step t will use
+          // release the TMEM buffer step t will use (dV / dK of step t - NB)
           while (ok && next <= t - C::NB) ok = dvdk(next++);
           if (!ok) break;
           const int gt = g0 + t;
@@ -265,7 +270,6 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
           }
           mma_commit(&bar_s[bb]);
           if (t == itm.n - 1) mma_commit(&bar_kv_empty[kvb]);  // last read of K/V
-          while (ok && next <= t - 1) ok = dvdk(next++);
         }
         while (ok && next < itm.n) ok = dvdk(next++);
         if (!ok) break;
@@ -300,8 +304,8 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
         tc_fence_after();
         const int it = itm.it0 + t;
         const int qc0 = (itm.qt_lo + it % itm.n_qtr) * 64 + grp * CPG;  // first query column
-        const uint32_t tP = tmem + C::P_COL + bb * 32 + grp * (CPG / 2) + lane_off;
-        const uint32_t tdS = tmem + C::DS_COL + bb * 32 + grp * (CPG / 2) + lane_off;
+        const uint32_t tP = tmem + C::S_COL + bb * 64 + grp * CPG + lane_off;  // over this group's S^T
+        const uint32_t tdS = tP + CPG / 2;
         if (block_none_visible(qc0, qc0 + CPG, kw0, kw0 + 32, W, S, L)) {
           const uint32_t z[8] = {0u};
           tmem_st8(tP, z);
