@@ -5,10 +5,13 @@
     torchrun --nproc-per-node N bench.py --gpus N ...
 
 Metric: effective TFLOP/s of fwd+bwd counting only useful (window + sink) FLOPs
-(14 * D per visible (query, key) pair), whole job over all ranks.  Multi-GPU runs are weak
-scaling: every rank owns its own batch shard of the workload (independent (batch, KV-head)
-units, no collective on the data path); the barrier and the max-over-ranks device time are
-the only cross-rank traffic.
+(14 * D per visible (query, key) pair), whole job over all ranks.  Work is partitioned by
+independent (batch, KV head) units with no collective on the data path; the barrier and the
+max-over-ranks device time are the only cross-rank traffic.
+  --scaling weak   (default) every rank runs its own full copy of the workload's shape
+                   (global batch = N x B);
+  --scaling strong the workload is fixed and its units are split over the ranks (e.g.
+                   cfg4_long_swa: 8 KV heads over 1/2/4/8 GPUs).
 
 Prints ONE JSON line (rank 0).
 """
@@ -31,6 +34,7 @@ sys.path.insert(0, ROOT)
 PKG = importlib.import_module("flashattention-gpt-oss-finetuning_b200")
 wl = importlib.import_module("flashattention-gpt-oss-finetuning_b200.workloads")
 plan_mod = importlib.import_module("flashattention-gpt-oss-finetuning_b200.plan")
+sh_mod = importlib.import_module("flashattention-gpt-oss-finetuning_b200.sharding")
 
 METRIC = "fwd+bwd effective TFLOP/s (window+sink FLOPs only)"
 UNIT = "TFLOP/s"
@@ -171,7 +175,7 @@ def run_reference(args, w, rank, world):
 # ---------------------------------------------------------------------------------------
 
 def device_timed(w, dev, rank, steps, warmup):
-    q, k, v, do = wl.make_inputs(w.replace(seed=w.seed + 1000 * rank), device=dev)
+    q, k, v, do = wl.make_inputs(w, device=dev)
     plan = plan_mod.SwaPlan(q, k, v, w.window_size, w.sink_size, None, dout=do)
     stream = torch.cuda.current_stream(dev)
     phases = ("fwd", "bwd_preprocess", "bwd_dkdv", "bwd_dq")
@@ -205,7 +209,7 @@ def device_timed(w, dev, rank, steps, warmup):
 
 def e2e_timed(w, dev, rank, steps, warmup):
     """Public API (autograd Function) with pinned host buffers, copies inside the timed region."""
-    q, k, v, do = (t.pin_memory() for t in wl.make_inputs(w.replace(seed=w.seed + 1000 * rank)))
+    q, k, v, do = (t.pin_memory() for t in wl.make_inputs(w))
     outs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (q, q, k, v)]
     stream = torch.cuda.current_stream(dev)
     h2d = sum(t.numel() * t.element_size() for t in (q, k, v, do))
@@ -242,7 +246,18 @@ def max_over_ranks(x: float, dev) -> float:
     return float(t.item())
 
 
-def run_ours(args, w, rank, world, local_rank):
+def rank_workload(w, rank, world, scaling):
+    """This rank's share: its own copy (weak) or its (batch, KV head) units (strong), the
+    units repacked as a batch of single-KV-head problems."""
+    if scaling == "weak" or world == 1:
+        return w.replace(seed=w.seed + 1000 * rank)
+    units = sh_mod.plan_units(w.batch, w.n_kv_heads, world)[rank]
+    return w.replace(batch=max(len(units), 1), n_q_heads=w.group, n_kv_heads=1,
+                     seed=w.seed + 1000 * rank)
+
+
+def run_ours(args, w_job, rank, world, local_rank):
+    w = rank_workload(w_job, rank, world, args.scaling)
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     hbm_peak, tf_peak, peak_kind = _peaks()
@@ -253,7 +268,7 @@ def run_ours(args, w, rank, world, local_rank):
     clk = clocks.stop() if clocks else None
     total_ms = max_over_ranks(total_ms, dev)
     ms = total_ms / args.steps
-    flops_job = wl.useful_flops(w) * world
+    flops_job = wl.useful_flops(w_job) * (world if args.scaling == "weak" else 1)
     value = flops_job / (ms * 1e-3) / 1e12
 
     e2e = None
@@ -287,10 +302,11 @@ def run_ours(args, w, rank, world, local_rank):
                 hbm_frac=(kw["bytes"] / t_s / 1e9) / hbm_peak)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": str(w.dtype).replace("torch.", "").replace("bfloat16", "bf16").replace("float16", "f16"),
         "data": "synthetic (seeded randn of the workload's shape; no dataset)",
-        "config": dict(w.describe(), global_batch=w.batch * world, parallelism=f"dp{world} by (batch, kv_head) units",
+        "config": dict(w_job.describe(), global_batch=w_job.batch * (world if args.scaling == "weak" else 1),
+                       per_rank=w.describe(), parallelism=f"dp{world} by (batch, kv_head) units",
                        l2="inputs larger than L2 (q, dO 134 MB each + k, v, o, grads)"),
         "phase_ms": per_phase,
         "gpu_launches": launches,
@@ -315,6 +331,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="cfg2_gptoss_swa", choices=sorted(wl.CONFIGS))
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

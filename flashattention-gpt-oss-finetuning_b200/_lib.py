@@ -29,6 +29,7 @@ EXPORTED_SYMBOLS = (
     "swa_fwd", "swa_bwd", "swa_bwd_preprocess", "swa_bwd_dq", "swa_bwd_dkdv",
     "swa_bwd_workspace_size", "swa_bwd_no_alloc", "swa_check_device",
     "swa_status_string", "swa_last_cuda_error", "swa_version", "swa_lse_row_stride",
+    "swa_selftest_wait_timeout",
 )
 
 
@@ -99,6 +100,8 @@ def _declare(l):
     l.swa_status_string.restype = ctypes.c_char_p
     l.swa_last_cuda_error.argtypes = []
     l.swa_last_cuda_error.restype = ctypes.c_char_p
+    l.swa_selftest_wait_timeout.argtypes = [ctypes.c_int, ctypes.c_void_p]
+    l.swa_selftest_wait_timeout.restype = ctypes.c_int
     l.swa_lse_row_stride.argtypes = [ctypes.c_int]
     l.swa_lse_row_stride.restype = ctypes.c_int
     l.swa_version.argtypes = []

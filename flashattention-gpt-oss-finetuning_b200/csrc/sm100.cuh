@@ -68,16 +68,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait for the phase with the given parity to complete.  Returns false (and the
 // caller must abandon its work) when the limit passes or `abort` has been raised.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                             uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (*abort) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) return false;
+      if (globaltimer() - t0 > limit_ns) return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  return mbar_wait_ns(bar, parity, abort, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------------------------------

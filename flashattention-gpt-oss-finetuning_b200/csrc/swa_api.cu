@@ -11,6 +11,7 @@
 
 namespace swa {
 template <typename T, int D> cudaError_t launch_fwd_tc(const FwdParams&, cudaStream_t, int*);
+cudaError_t launch_selftest_wait_timeout(int* err, unsigned long long limit_ns, cudaStream_t st);
 template <typename T, int D> cudaError_t launch_bwd_preprocess(const BwdParams&, cudaStream_t);
 template <typename T, int D> cudaError_t launch_bwd_dq_tc(const BwdParams&, cudaStream_t, int*);
 template <typename T, int D> cudaError_t launch_bwd_dkdv_tc(const BwdParams&, cudaStream_t, int*);
@@ -198,6 +199,14 @@ int swa_check_device(void* stream) {
   e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
   if (e != cudaSuccess) return record(e);
   return SWA_ERR_DEVICE_TIMEOUT;
+}
+
+int swa_selftest_wait_timeout(int limit_us, void* stream) {
+  if (limit_us <= 0 || limit_us > 1000000) return SWA_ERR_INVALID_ARG;
+  int* err = device_error_ptr();
+  if (!err) return SWA_ERR_LAUNCH;
+  return record(swa::launch_selftest_wait_timeout(err, 1000ull * (unsigned long long)limit_us,
+                                                  static_cast<cudaStream_t>(stream)));
 }
 
 size_t swa_bwd_workspace_size(const SwaProblem* p) {

@@ -51,6 +51,8 @@ class SwaPlan:
         self._ba = ctypes.byref(self.bwd_args)
         self.device = q.device
         self.launches = 0
+        # swa_bwd_dkdv launches a second (sink-row reduction) kernel when there are sinks
+        self._dkdv_kernels = 2 if min(int(sink_size), q.shape[2]) > 0 else 1
 
     def _s(self, stream) -> int:
         return (stream or torch.cuda.current_stream(self.device)).cuda_stream
@@ -65,7 +67,7 @@ class SwaPlan:
 
     def bwd_dkdv(self, stream=None):
         _lib.check(self.lib.swa_bwd_dkdv(self._ba, self._s(stream)), "swa_bwd_dkdv")
-        self.launches += 1
+        self.launches += self._dkdv_kernels
 
     def bwd_dq(self, stream=None):
         _lib.check(self.lib.swa_bwd_dq(self._ba, self._s(stream)), "swa_bwd_dq")

@@ -137,6 +137,12 @@ SWA_API int swa_bwd_no_alloc(const SwaBwdArgs* args, void* stream);
  * (that launch's outputs are then undefined), SWA_OK otherwise. */
 SWA_API int swa_check_device(void* stream);
 
+/* Failure-path self-test: launches a kernel whose bounded on-device wait (on a barrier that
+ * nothing arrives at) gives up after `limit_us` microseconds (1 .. 1e6) and records the
+ * error; a following swa_check_device returns SWA_ERR_DEVICE_TIMEOUT.  No counterpart in the
+ * reference (its kernels have no bounded waits). */
+SWA_API int swa_selftest_wait_timeout(int limit_us, void* stream);
+
 /* Human-readable name of a SwaStatus. */
 SWA_API const char* swa_status_string(int status);
 

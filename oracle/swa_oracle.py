@@ -169,3 +169,38 @@ def useful_flops(b, hq, seq_len, d, window_size, sink_size, which="fwd+bwd") -> 
     pairs = b * hq * visible_pairs_per_head(seq_len, window_size, sink_size)
     per = {"fwd": 4, "bwd": 10, "fwd+bwd": 14}[which]
     return float(per * d * pairs)
+
+
+# --------------------------------------------------------------------------------------
+# Windowed oracle for very long sequences (one query head / KV head pair, [L, D] tensors)
+# --------------------------------------------------------------------------------------
+
+def rows_backward(qh, kh, vh, doh, r0: int, r1: int, window_size: int, sink_size: int,
+                  scale: Optional[float] = None, compute_dtype=torch.float64):
+    """Exact O, dQ for query rows [r0, r1) using only the keys they can see, plus the dense
+    P and dS over those keys (for dK / dV contributions).
+
+    The same algebra as :func:`backward` (benchmark_backward_speed.py:68-85 and its autograd
+    gradient), restricted to the key set sinks [0, S) U window [r0 - W + 1, r1).  Returns
+    (o [R, D], dq [R, D], keys [K] (absolute indices), p [R, K], ds [R, K]); ds excludes the
+    softmax scale (dK_j = scale * sum_i ds_ij q_i).
+    """
+    L, d = qh.shape
+    sc = _scale(d, scale)
+    w = max(0, int(window_size))
+    lo = max(0, r0 - w + 1)
+    keys = sorted(set(range(min(sink_size, r1))) | set(range(lo, r1)))
+    keys_t = torch.tensor(keys, dtype=torch.long)
+    q = qh[r0:r1].to(compute_dtype)
+    do = doh[r0:r1].to(compute_dtype)
+    k = kh[keys_t].to(compute_dtype)
+    v = vh[keys_t].to(compute_dtype)
+    i = torch.arange(r0, r1)[:, None]
+    j = keys_t[None, :]
+    mask = (j <= i) & ((i - j < w) | (j < sink_size))
+    p, _ = _probs(q, k, mask, sc, "zero")
+    o = p @ v
+    delta = (do * o).sum(-1, keepdim=True)
+    ds = p * (do @ v.transpose(-1, -2) - delta)
+    dq = (ds @ k) * sc
+    return o, dq, keys_t, p, ds
