@@ -320,8 +320,9 @@ def run_ours(args, w_job, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
-# DRAM bytes (read + write) per launch from one ncu capture, keyed by (workload, kernel).
-TRAFFIC: dict = {}
+# DRAM bytes (read + write) per launch from one ncu capture, keyed by (workload, kernel)
+# (profiles/dkdv_tc_cfg2_ncu.md: 576.5 MB read + 27.1 MB written).
+TRAFFIC: dict = {("cfg2_gptoss_swa", "bwd_dkdv"): 603_651_584}
 
 
 def main():
