@@ -151,6 +151,10 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t smem_addr, uint32_t lbo, uint
   return d;
 }
 
+// Descriptor of the same layout starting `bytes` further on (the 14-bit start-address field
+// cannot carry: every shared-memory address is below 256 KB).
+__device__ __forceinline__ uint64_t sdesc_add(uint64_t d, uint32_t bytes) { return d + (bytes >> 4); }
+
 // Instruction descriptor for kind::f16 with fp32 accumulation.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool a_mn_major,
                                                  bool b_mn_major) {

@@ -174,6 +174,8 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0 && !dead) {
       constexpr uint32_t id_q = idesc_f16(128, D, kBf16, false, true);  // dQ += dS K
+      const uint64_t it0 = sdesc(saddr(ITs), 16, 8 * C::ROWB, C::SWZ);            // item 0: Q (K-major)
+      const uint64_t kv0 = sdesc(saddr(KVs), 16, 8 * C::ROWB, C::SWZ);            // stage 0: K (K-major)
       int qi = 0, gs = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
@@ -184,8 +186,7 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
         if (n == 0) continue;
         const int qb = qi % C::NQB;
         if (!(ok = mbar_wait(&bar_q_full[qb], (qi / C::NQB) & 1, &abort_sh))) break;
-        const unsigned char* Qb = ITs + qb * C::ITEM;
-        const unsigned char* dOb = Qb + C::QT_BYTES;
+        const uint64_t dQa = sdesc_add(it0, qb * C::ITEM), dOa = sdesc_add(dQa, C::QT_BYTES);
         const int g0 = gs;
         int next = 0;
         auto dq_mma = [&](int u) -> bool {
@@ -198,9 +199,9 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
           int key0, rows;
           sc.seg(u, &key0, &rows);
           const int st = gu % C::NST;
-          const unsigned char* Kb = KVs + st * 2 * C::KV_BYTES;
+          const uint64_t kmn = sdesc(saddr(KVs + st * 2 * C::KV_BYTES), rows * C::ROWB, 8 * C::ROWB, C::SWZ);
           for (int ks = 0; ks < rows / 16; ++ks) {
-            const uint64_t bk = sdesc(saddr(Kb + ks * 16 * C::ROWB), rows * C::ROWB, 8 * C::ROWB, C::SWZ);
+            const uint64_t bk = sdesc_add(kmn, ks * 16 * C::ROWB);
             mma_ts(tmem + C::DQ_COL, tmem + C::S_COL + bb * 64 + ks * 16, bk, id_q, (u > 0 || ks > 0) ? 1u : 0u);
           }
           mma_commit(&bar_empty[st]);
@@ -215,16 +216,15 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
           tc_fence_after();
           int key0, rows;
           sc.seg(t, &key0, &rows);
-          const unsigned char* Kb = KVs + st * 2 * C::KV_BYTES;
-          const unsigned char* Vb = Kb + C::KV_BYTES;
+          const uint64_t kk = sdesc_add(kv0, st * 2 * C::KV_BYTES), vk = sdesc_add(kk, C::KV_BYTES);
           const uint32_t id_s = idesc_f16(128, rows, kBf16, false, false);
 #pragma unroll
           for (int ks = 0; ks < D / 16; ++ks) {
             const int ch = (ks * 16) / C::CW, within = (ks * 16) % C::CW;
-            const uint64_t aq = sdesc(saddr(Qb + ch * C::BM * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
-            const uint64_t ado = sdesc(saddr(dOb + ch * C::BM * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
-            const uint64_t bk = sdesc(saddr(Kb + ch * rows * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
-            const uint64_t bv = sdesc(saddr(Vb + ch * rows * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
+            const uint64_t aq = sdesc_add(dQa, ch * C::BM * C::ROWB + within * 2);
+            const uint64_t ado = sdesc_add(dOa, ch * C::BM * C::ROWB + within * 2);
+            const uint64_t bk = sdesc_add(kk, ch * rows * C::ROWB + within * 2);
+            const uint64_t bv = sdesc_add(vk, ch * rows * C::ROWB + within * 2);
             mma_ss(tmem + C::S_COL + bb * 64, aq, bk, id_s, ks > 0 ? 1u : 0u);
             mma_ss(tmem + C::DP_COL + bb * 64, ado, bv, id_s, ks > 0 ? 1u : 0u);
           }

@@ -17,12 +17,13 @@
 //   dV  += P^T dO     (A = P^T from TMEM, B = dO MN-major smem)
 //   dK  += dS^T Q     (A = dS^T from TMEM, B = Q MN-major smem)
 // S^T and dP^T have NB = 3 TMEM buffers (2 for D = 128); P^T and dS^T are written back over
-// the S^T columns each elementwise warp has read.  The MMA thread issues S^T / dP^T of step t
-// as soon as step t - NB's buffer is released and the dV / dK MMAs of a step only just
-// before its buffer is reused, so S^T runs up to NB - 1 steps ahead of the elementwise warps.
+// the S^T columns each elementwise warp has read.  S^T / dP^T of step t are issued as soon as
+// the dV / dK MMAs of step t - NB (which read that buffer's P^T / dS^T) have completed, so
+// S^T runs up to NB - 1 steps ahead of the elementwise warps.
 //
 // Warp roles (20 warps, 640 threads): warp 0 TMA producer (K/V per item, Q/dO + LSE/Delta per
-// step), warp 1 MMA issuer (one thread), warps 4..19 elementwise + epilogue: four warps per
+// step), warp 1 issues the S^T / dP^T MMAs and warp 2 the dV / dK MMAs (one thread each, so
+// neither waits behind the other's barrier), warps 4..19 elementwise + epilogue: four warps per
 // TMEM lane quadrant, 16 query columns each (no row reductions are needed in the backward,
 // so the split costs nothing and gives every scheduler four independent warps).
 // Every mbarrier wait is bounded; a wait that gives up records an error and the CTA exits.
@@ -118,7 +119,7 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
 
   __shared__ uint64_t bar_kv_full[C::NKV], bar_kv_empty[C::NKV];
   __shared__ uint64_t bar_full[C::NST], bar_empty[C::NST];
-  __shared__ uint64_t bar_s[C::NB], bar_p[C::NB], bar_acc, bar_acc_free;
+  __shared__ uint64_t bar_s[C::NB], bar_p[C::NB], bar_rel[C::NB], bar_acc, bar_acc_free;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
 
@@ -141,6 +142,7 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
       mbar_init(&bar_empty[s], 1);
     }
     for (int s = 0; s < C::NB; ++s) {
+      mbar_init(&bar_rel[s], 1);
       mbar_init(&bar_s[s], 1);
       mbar_init(&bar_p[s], 128 * C::NGRP);
     }
@@ -211,10 +213,10 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------------ MMA issuer: S^T, dP^T
     if (lane == 0 && !dead) {
-      constexpr uint32_t id_s = idesc_f16(128, 64, kBf16, false, false);  // S^T, dP^T
-      constexpr uint32_t id_a = idesc_f16(128, D, kBf16, false, true);    // dV, dK
+      constexpr uint32_t id_s = idesc_f16(128, 64, kBf16, false, false);
+      const uint64_t qk0 = sdesc(saddr(STs), 16, 8 * C::ROWB, C::SWZ);  // stage 0 Q, K-major
       int qi = 0, gs = 0;
       bool ok = true;
       for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
@@ -222,56 +224,67 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
         if (itm.n == 0) continue;
         const int kvb = qi % C::NKV;
         if (!(ok = mbar_wait(&bar_kv_full[kvb], (qi / C::NKV) & 1, &abort_sh))) break;
-        const unsigned char* Kb = KVs + kvb * 2 * C::KV_BYTES;
-        const unsigned char* Vb = Kb + C::KV_BYTES;
-        const int g0 = gs;  // global index of the item's first step
-        int next = 0;       // next step of this item whose dV/dK MMAs are due
-        auto dvdk = [&](int u) -> bool {
-          const int gu = g0 + u;
-          const int bb = gu % C::NB;
-          if (!mbar_wait(&bar_p[bb], (gu / C::NB) & 1, &abort_sh)) return false;
-          // the previous item's epilogue must have read dK/dV before they are overwritten
-          if (u == 0 && qi > 0 && !mbar_wait(&bar_acc_free, (qi - 1) & 1, &abort_sh)) return false;
-          tc_fence_after();
-          const int st = gu % C::NST;
-          const unsigned char* Qb = STs + st * C::STAGE;
-          const unsigned char* dOb = Qb + C::QT_BYTES;
-          const uint32_t tS = tmem + C::S_COL + bb * 64;
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {  // K = 64 query rows, 16 per MMA
-            const uint64_t bdo = sdesc(saddr(dOb + ks * 16 * C::ROWB), 64 * C::ROWB, 8 * C::ROWB, C::SWZ);
-            const uint64_t bq = sdesc(saddr(Qb + ks * 16 * C::ROWB), 64 * C::ROWB, 8 * C::ROWB, C::SWZ);
-            const uint32_t acc = (u > 0 || ks > 0) ? 1u : 0u;
-            mma_ts(tmem + C::DV_COL, tS + ks * 16, bdo, id_a, acc);
-            mma_ts(tmem + C::DK_COL, tS + ks * 16 + 8, bq, id_a, acc);
-          }
-          mma_commit(&bar_empty[st]);
-          return true;
-        };
-        for (int t = 0; t < itm.n && ok; ++t) {
-          // release the TMEM buffer step t will use (dV / dK of step t - NB)
-          while (ok && next <= t - C::NB) ok = dvdk(next++);
-          if (!ok) break;
-          const int gt = g0 + t;
+        const uint64_t dK0 = sdesc(saddr(KVs + kvb * 2 * C::KV_BYTES), 16, 8 * C::ROWB, C::SWZ);
+        const uint64_t dV0 = sdesc_add(dK0, C::KV_BYTES);
+        for (int t = 0; t < itm.n; ++t) {
+          const int gt = gs + t;
           const int st = gt % C::NST, bb = gt % C::NB;
+          // TMEM buffer bb is free once the dV/dK MMAs of step gt - NB have completed
+          if (gt >= C::NB && !(ok = mbar_wait(&bar_rel[bb], ((gt - C::NB) / C::NB) & 1, &abort_sh))) break;
           if (!(ok = mbar_wait(&bar_full[st], (gt / C::NST) & 1, &abort_sh))) break;
           tc_fence_after();
-          const unsigned char* Qb = STs + st * C::STAGE;
-          const unsigned char* dOb = Qb + C::QT_BYTES;
+          const uint64_t qk = sdesc_add(qk0, st * C::STAGE), dok = sdesc_add(qk, C::QT_BYTES);
 #pragma unroll
           for (int ks = 0; ks < D / 16; ++ks) {
             const int ch = (ks * 16) / C::CW, within = (ks * 16) % C::CW;
-            const uint64_t ak = sdesc(saddr(Kb + ch * 128 * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
-            const uint64_t av = sdesc(saddr(Vb + ch * 128 * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
-            const uint64_t bq = sdesc(saddr(Qb + ch * 64 * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
-            const uint64_t bdo = sdesc(saddr(dOb + ch * 64 * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
+            const uint64_t ak = sdesc_add(dK0, ch * 128 * C::ROWB + within * 2);
+            const uint64_t av = sdesc_add(dV0, ch * 128 * C::ROWB + within * 2);
+            const uint64_t bq = sdesc_add(qk, ch * 64 * C::ROWB + within * 2);
+            const uint64_t bdo = sdesc_add(dok, ch * 64 * C::ROWB + within * 2);
             mma_ss(tmem + C::S_COL + bb * 64, ak, bq, id_s, ks > 0 ? 1u : 0u);
             mma_ss(tmem + C::DP_COL + bb * 64, av, bdo, id_s, ks > 0 ? 1u : 0u);
           }
           mma_commit(&bar_s[bb]);
           if (t == itm.n - 1) mma_commit(&bar_kv_empty[kvb]);  // last read of K/V
         }
-        while (ok && next < itm.n) ok = dvdk(next++);
+        gs += itm.n;
+        ++qi;
+      }
+      if (!ok) {
+        abort_sh = 1;
+        record_error(err, 1);
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ MMA issuer: dV, dK
+    if (lane == 0 && !dead) {
+      constexpr uint32_t id_a = idesc_f16(128, D, kBf16, false, true);
+      const uint64_t qmn0 = sdesc(saddr(STs), 64 * C::ROWB, 8 * C::ROWB, C::SWZ);  // stage 0 Q, MN-major
+      int qi = 0, gs = 0;
+      bool ok = true;
+      for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+        const DkdvItem itm = dkdv_item(idx, p, G, n_kt, n_qt);
+        if (itm.n == 0) continue;
+        for (int u = 0; u < itm.n; ++u) {
+          const int gu = gs + u;
+          const int bb = gu % C::NB, st = gu % C::NST;
+          if (!(ok = mbar_wait(&bar_p[bb], (gu / C::NB) & 1, &abort_sh))) break;
+          // the previous item's epilogue must have read dK/dV before they are overwritten
+          if (u == 0 && qi > 0 && !(ok = mbar_wait(&bar_acc_free, (qi - 1) & 1, &abort_sh))) break;
+          tc_fence_after();
+          const uint64_t qmn = sdesc_add(qmn0, st * C::STAGE), domn = sdesc_add(qmn, C::QT_BYTES);
+          const uint32_t tS = tmem + C::S_COL + bb * 64;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {  // K = 64 query rows, 16 per MMA
+            const uint64_t bdo = sdesc_add(domn, ks * 16 * C::ROWB);
+            const uint64_t bq = sdesc_add(qmn, ks * 16 * C::ROWB);
+            const uint32_t acc = (u > 0 || ks > 0) ? 1u : 0u;
+            mma_ts(tmem + C::DV_COL, tS + ks * 16, bdo, id_a, acc);
+            mma_ts(tmem + C::DK_COL, tS + ks * 16 + 8, bq, id_a, acc);
+          }
+          mma_commit(&bar_empty[st]);
+          mma_commit(&bar_rel[bb]);
+        }
         if (!ok) break;
         mma_commit(&bar_acc);
         gs += itm.n;

@@ -255,6 +255,8 @@ __global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
     // Flattened sequence of (item, segment) pairs; S of pair g+1 is issued before PV of g.
     if (lane == 0 && !dead) {
       constexpr uint32_t id_o = idesc_f16(128, D, kBf16, false, true);
+      const uint64_t q_desc0 = sdesc(saddr(Qs), 16, 8 * C::ROWB, C::SWZ);    // Q buffer 0, K-major
+      const uint64_t kv_desc0 = sdesc(saddr(KVs), 16, 8 * C::ROWB, C::SWZ);  // K stage 0, K-major
       bool ok = true;
       int s_it = blockIdx.x, s_t = 0, s_qi = 0, s_n = 0, s_g = 0;  // S cursor
       FwdSched s_sc;
@@ -280,15 +282,15 @@ __global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
         tc_fence_after();
         int key0, rows;
         s_sc.seg(s_t, &key0, &rows);
-        const unsigned char* Qb = Qs + qb * C::Q_BYTES;
-        const unsigned char* Kb = KVs + st * 2 * C::KV_BYTES;
+        const uint64_t qd = sdesc_add(q_desc0, qb * C::Q_BYTES);
+        const uint64_t kd = sdesc_add(kv_desc0, st * 2 * C::KV_BYTES);
         const uint32_t id_s = idesc_f16(128, rows, kBf16, false, false);
         const uint32_t tS = tmem + C::S_COL + (s_g & 1) * 64;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const int ch = (ks * 16) / C::CW, within = (ks * 16) % C::CW;
-          const uint64_t ad = sdesc(saddr(Qb + ch * C::BM * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
-          const uint64_t bd = sdesc(saddr(Kb + ch * rows * C::ROWB + within * 2), 16, 8 * C::ROWB, C::SWZ);
+          const uint64_t ad = sdesc_add(qd, ch * C::BM * C::ROWB + within * 2);
+          const uint64_t bd = sdesc_add(kd, ch * rows * C::ROWB + within * 2);
           mma_ss(tS, ad, bd, id_s, ks > 0 ? 1u : 0u);
         }
         mma_commit(&bar_s[s_g & 1]);
@@ -314,10 +316,10 @@ __global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
         int key0, rows;
         v_sc.seg(v_t, &key0, &rows);
         const int st = v_g % C::NST;
-        const unsigned char* Vb = KVs + st * 2 * C::KV_BYTES + C::KV_BYTES;
+        const uint64_t vd = sdesc(saddr(KVs + st * 2 * C::KV_BYTES + C::KV_BYTES), rows * C::ROWB, 8 * C::ROWB, C::SWZ);
         const uint32_t tP = tmem + C::P_COL + (v_g & 1) * 32;
         for (int ks = 0; ks < rows / 16; ++ks) {
-          const uint64_t bd = sdesc(saddr(Vb + ks * 16 * C::ROWB), rows * C::ROWB, 8 * C::ROWB, C::SWZ);
+          const uint64_t bd = sdesc_add(vd, ks * 16 * C::ROWB);
           mma_ts(tmem + C::O_COL, tP + ks * 8, bd, id_o, (v_t > 0 || ks > 0) ? 1u : 0u);
         }
         mma_commit(&bar_empty[st]);
