@@ -9,16 +9,17 @@
 //        (warps 4..19: each thread owns one query row and 16 key columns)
 //   dQ += dS K                     (A = dS from TMEM, B = K MN-major smem) -> TMEM
 // and dQ * scale is written once per item.  S and dP have NB = 3 TMEM buffers (2 for
-// D = 128) and dS is written back over the S columns each warp has read; the dQ MMAs of a
-// segment are issued just before its buffer is reused, so S runs ahead of the elementwise
-// warps.
+// D = 128) and dS is written back over the S columns each warp has read; S / dP of segment t
+// are issued as soon as the dQ MMAs of segment t - NB have completed, so S runs ahead of the
+// elementwise warps.
 //
 // Reference behaviour followed: the dQ part of _flash_attention_backward_swa_kernel
 // (flash_attention_gpt_oss.py:306-321, 334-338), restricted to the visible key segments
 // (the reference loops over all L keys).  LSE and Delta rows come from the padded
 // [B, Hq, round_up(L, 64)] buffers (+inf / 0 past L), so padded query rows contribute zero.
 //
-// Warp roles (20 warps, 640 threads): warp 0 TMA producer, warp 1 MMA issuer (one thread),
+// Warp roles (20 warps, 640 threads): warp 0 TMA producer, warp 1 issues the S / dP MMAs and
+// warp 2 the dQ MMAs (one thread each; a buffer-release barrier orders them),
 // warps 4..19 elementwise + epilogue: four warps per TMEM lane quadrant, 16 key columns each,
 // so that every scheduler has four independent elementwise warps to hide the TMEM and
 // special-function latencies.  Every mbarrier wait is bounded.
@@ -78,7 +79,7 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
 
   __shared__ uint64_t bar_q_full[C::NQB], bar_q_empty[C::NQB];
   __shared__ uint64_t bar_full[C::NST], bar_empty[C::NST];
-  __shared__ uint64_t bar_s[C::NB], bar_p[C::NB], bar_acc, bar_acc_free;
+  __shared__ uint64_t bar_s[C::NB], bar_p[C::NB], bar_rel[C::NB], bar_acc, bar_acc_free;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
 
@@ -100,6 +101,7 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
       mbar_init(&bar_empty[s], 1);
     }
     for (int s = 0; s < C::NB; ++s) {
+      mbar_init(&bar_rel[s], 1);
       mbar_init(&bar_s[s], 1);
       mbar_init(&bar_p[s], 128 * C::NGRP);
     }
@@ -171,11 +173,10 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------------ MMA issuer: S, dP
     if (lane == 0 && !dead) {
-      constexpr uint32_t id_q = idesc_f16(128, D, kBf16, false, true);  // dQ += dS K
-      const uint64_t it0 = sdesc(saddr(ITs), 16, 8 * C::ROWB, C::SWZ);            // item 0: Q (K-major)
-      const uint64_t kv0 = sdesc(saddr(KVs), 16, 8 * C::ROWB, C::SWZ);            // stage 0: K (K-major)
+      const uint64_t it0 = sdesc(saddr(ITs), 16, 8 * C::ROWB, C::SWZ);  // item 0: Q (K-major)
+      const uint64_t kv0 = sdesc(saddr(KVs), 16, 8 * C::ROWB, C::SWZ);  // stage 0: K (K-major)
       int qi = 0, gs = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
@@ -187,31 +188,11 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
         const int qb = qi % C::NQB;
         if (!(ok = mbar_wait(&bar_q_full[qb], (qi / C::NQB) & 1, &abort_sh))) break;
         const uint64_t dQa = sdesc_add(it0, qb * C::ITEM), dOa = sdesc_add(dQa, C::QT_BYTES);
-        const int g0 = gs;
-        int next = 0;
-        auto dq_mma = [&](int u) -> bool {
-          const int gu = g0 + u;
-          const int bb = gu % C::NB;
-          if (!mbar_wait(&bar_p[bb], (gu / C::NB) & 1, &abort_sh)) return false;
-          // the previous item's epilogue must have read dQ before it is overwritten
-          if (u == 0 && qi > 0 && !mbar_wait(&bar_acc_free, (qi - 1) & 1, &abort_sh)) return false;
-          tc_fence_after();
-          int key0, rows;
-          sc.seg(u, &key0, &rows);
-          const int st = gu % C::NST;
-          const uint64_t kmn = sdesc(saddr(KVs + st * 2 * C::KV_BYTES), rows * C::ROWB, 8 * C::ROWB, C::SWZ);
-          for (int ks = 0; ks < rows / 16; ++ks) {
-            const uint64_t bk = sdesc_add(kmn, ks * 16 * C::ROWB);
-            mma_ts(tmem + C::DQ_COL, tmem + C::S_COL + bb * 64 + ks * 16, bk, id_q, (u > 0 || ks > 0) ? 1u : 0u);
-          }
-          mma_commit(&bar_empty[st]);
-          return true;
-        };
-        for (int t = 0; t < n && ok; ++t) {
-          while (ok && next <= t - C::NB) ok = dq_mma(next++);
-          if (!ok) break;
-          const int gt = g0 + t;
+        for (int t = 0; t < n; ++t) {
+          const int gt = gs + t;
           const int st = gt % C::NST, bb = gt % C::NB;
+          // TMEM buffer bb is free once the dQ MMAs of segment gt - NB have completed
+          if (gt >= C::NB && !(ok = mbar_wait(&bar_rel[bb], ((gt - C::NB) / C::NB) & 1, &abort_sh))) break;
           if (!(ok = mbar_wait(&bar_full[st], (gt / C::NST) & 1, &abort_sh))) break;
           tc_fence_after();
           int key0, rows;
@@ -230,11 +211,49 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
           }
           mma_commit(&bar_s[bb]);
         }
-        while (ok && next < n) ok = dq_mma(next++);
+        gs += n;
+        ++qi;
+      }
+      if (!ok) {
+        abort_sh = 1;
+        record_error(err, 1);
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ MMA issuer: dQ
+    if (lane == 0 && !dead) {
+      constexpr uint32_t id_q = idesc_f16(128, D, kBf16, false, true);  // dQ += dS K
+      int qi = 0, gs = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        int b, h, qt;
+        decode_item(it, Hq, n_qt, &b, &h, &qt);
+        const FwdSched sc = fwd_schedule(qt * C::BM, L, W, S, p.sink_box);
+        const int n = sc.n();
+        if (n == 0) continue;
+        const int qb = qi % C::NQB;
+        for (int u = 0; u < n; ++u) {
+          const int gu = gs + u;
+          const int bb = gu % C::NB, st = gu % C::NST;
+          if (!(ok = mbar_wait(&bar_p[bb], (gu / C::NB) & 1, &abort_sh))) break;
+          // the previous item's epilogue must have read dQ before it is overwritten
+          if (u == 0 && qi > 0 && !(ok = mbar_wait(&bar_acc_free, (qi - 1) & 1, &abort_sh))) break;
+          tc_fence_after();
+          int key0, rows;
+          sc.seg(u, &key0, &rows);
+          const uint64_t kmn = sdesc(saddr(KVs + st * 2 * C::KV_BYTES), rows * C::ROWB, 8 * C::ROWB, C::SWZ);
+          for (int ks = 0; ks < rows / 16; ++ks) {
+            const uint64_t bk = sdesc_add(kmn, ks * 16 * C::ROWB);
+            mma_ts(tmem + C::DQ_COL, tmem + C::S_COL + bb * 64 + ks * 16, bk, id_q, (u > 0 || ks > 0) ? 1u : 0u);
+          }
+          mma_commit(&bar_empty[st]);
+          mma_commit(&bar_rel[bb]);
+        }
         if (!ok) break;
         mma_commit(&bar_acc);
-        // Q / dO are free, and so are LSE / Delta (read by the elementwise warps before
-        // their first P barrier of the item)
+        // Q / dO are free (the S / dP MMAs finished before the elementwise pass, which came
+        // before this item's last P barrier), and so are LSE / Delta (read by the elementwise
+        // warps before their first P barrier of the item)
         mma_commit(&bar_q_empty[qb]);
         gs += n;
         ++qi;
