@@ -5,13 +5,15 @@
 // window: sink segments of SB keys (SB = S rounded up to 16, at most 64) below the window,
 // then 64-key window tiles.
 //
-// Warp roles (6 warps, 192 threads):
+// Warp roles (7 warps, 224 threads):
 //   warp 0   TMA producer: Q tiles (double-buffered) and K/V segments into a shared-memory
 //            ring, 128/64/32-byte swizzled (the UMMA canonical layouts); runs ahead across
 //            items.
-//   warp 1   MMA issuer (one thread): S_g = Q K_g^T into TMEM buffer g&1 one segment ahead of
-//            the softmax, then O += P_g V_g with P read from TMEM (A operand in TMEM) and V as
-//            an MN-major B operand.
+//   warp 1   S MMA issuer (one thread): S_g = Q K_g^T into TMEM buffer g&1, as soon as the
+//            softmax has read S_{g-2}.
+//   warp 6   PV MMA issuer (one thread): O += P_g V_g with P read from TMEM (A operand in
+//            TMEM) and V as an MN-major B operand.  The softmax waits for PV_{g-2} (per-buffer
+//            barrier) before overwriting P buffer g&1, and for PV_{g-1} before rescaling O.
 //   warps 2-5  softmax: thread t owns query row t (TMEM lane t).  Per 32-row warp block a
 //            segment that the block cannot see is skipped (P = 0) and one it sees completely
 //            is not masked.  O is rescaled in TMEM only when the row max grows by more than
@@ -155,7 +157,7 @@ __device__ __forceinline__ void softmax_segment(uint32_t tS_lane, uint32_t tP_la
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __grid_constant__ FwdTmaps tm,
+__global__ void __launch_bounds__(224, D <= 64 ? 2 : 1) fwd_tc_kernel(const __grid_constant__ FwdTmaps tm,
                                                                        const FwdParams p, int* err) {
   using C = FwdCfg<D>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -167,7 +169,7 @@ __global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
 
   __shared__ uint64_t bar_q_full[2], bar_q_empty[2];
   __shared__ uint64_t bar_full[C::NST], bar_empty[C::NST];
-  __shared__ uint64_t bar_s[2], bar_p[2], bar_pv, bar_o_full, bar_o_free;
+  __shared__ uint64_t bar_s[2], bar_p[2], bar_pv[2], bar_o_full, bar_o_free;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
 
@@ -187,12 +189,12 @@ __global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
       mbar_init(&bar_q_empty[s], 1);
       mbar_init(&bar_s[s], 1);
       mbar_init(&bar_p[s], 128);
+      mbar_init(&bar_pv[s], 1);
     }
     for (int s = 0; s < C::NST; ++s) {
       mbar_init(&bar_full[s], 1);
       mbar_init(&bar_empty[s], 1);
     }
-    mbar_init(&bar_pv, 1);
     mbar_init(&bar_o_full, 1);
     mbar_init(&bar_o_free, 128);
     fence_mbar_init();
@@ -251,94 +253,85 @@ __global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    // Flattened sequence of (item, segment) pairs; S of pair g+1 is issued before PV of g.
+    // ------------------------------------------------------------------ MMA issuer: S = Q K^T
     if (lane == 0 && !dead) {
-      constexpr uint32_t id_o = idesc_f16(128, D, kBf16, false, true);
       const uint64_t q_desc0 = sdesc(saddr(Qs), 16, 8 * C::ROWB, C::SWZ);    // Q buffer 0, K-major
       const uint64_t kv_desc0 = sdesc(saddr(KVs), 16, 8 * C::ROWB, C::SWZ);  // K stage 0, K-major
+      int qi = 0, g = 0;
       bool ok = true;
-      int s_it = blockIdx.x, s_t = 0, s_qi = 0, s_n = 0, s_g = 0;  // S cursor
-      FwdSched s_sc;
-      int v_it = blockIdx.x, v_t = 0, v_qi = 0, v_n = 0, v_g = 0;  // PV cursor
-      FwdSched v_sc;
-      auto next_item = [&](int& it, FwdSched& sc, int& n) -> bool {
-        for (; it < n_items; it += gridDim.x) {
-          int b, h, qt;
-          decode_item(it, Hq, n_qt, &b, &h, &qt);
-          sc = fwd_schedule(qt * C::BM, L, W, S, p.sink_box);
-          n = sc.n();
-          if (n > 0) return true;
-        }
-        return false;
-      };
-      bool s_more = next_item(s_it, s_sc, s_n);
-      bool v_more = next_item(v_it, v_sc, v_n);
-      auto issue_s = [&]() -> bool {
-        const int qb = s_qi & 1;
-        if (s_t == 0 && !mbar_wait(&bar_q_full[qb], (s_qi >> 1) & 1, &abort_sh)) return false;
-        const int st = s_g % C::NST;
-        if (!mbar_wait(&bar_full[st], (s_g / C::NST) & 1, &abort_sh)) return false;
-        tc_fence_after();
-        int key0, rows;
-        s_sc.seg(s_t, &key0, &rows);
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        int b, h, qt;
+        decode_item(it, Hq, n_qt, &b, &h, &qt);
+        const FwdSched sc = fwd_schedule(qt * C::BM, L, W, S, p.sink_box);
+        const int n = sc.n();
+        if (n == 0) continue;
+        const int qb = qi & 1;
+        if (!(ok = mbar_wait(&bar_q_full[qb], (qi >> 1) & 1, &abort_sh))) break;
         const uint64_t qd = sdesc_add(q_desc0, qb * C::Q_BYTES);
-        const uint64_t kd = sdesc_add(kv_desc0, st * 2 * C::KV_BYTES);
-        const uint32_t id_s = idesc_f16(128, rows, kBf16, false, false);
-        const uint32_t tS = tmem + C::S_COL + (s_g & 1) * 64;
+        for (int t = 0; t < n; ++t, ++g) {
+          // S buffer g&1 is free once the softmax has read S of segment g - 2
+          if (g >= 2 && !(ok = mbar_wait(&bar_p[g & 1], ((g - 2) >> 1) & 1, &abort_sh))) break;
+          const int st = g % C::NST;
+          if (!(ok = mbar_wait(&bar_full[st], (g / C::NST) & 1, &abort_sh))) break;
+          tc_fence_after();
+          int key0, rows;
+          sc.seg(t, &key0, &rows);
+          const uint64_t kd = sdesc_add(kv_desc0, st * 2 * C::KV_BYTES);
+          const uint32_t id_s = idesc_f16(128, rows, kBf16, false, false);
+          const uint32_t tS = tmem + C::S_COL + (g & 1) * 64;
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) {
-          const int ch = (ks * 16) / C::CW, within = (ks * 16) % C::CW;
-          const uint64_t ad = sdesc_add(qd, ch * C::BM * C::ROWB + within * 2);
-          const uint64_t bd = sdesc_add(kd, ch * rows * C::ROWB + within * 2);
-          mma_ss(tS, ad, bd, id_s, ks > 0 ? 1u : 0u);
+          for (int ks = 0; ks < D / 16; ++ks) {
+            const int ch = (ks * 16) / C::CW, within = (ks * 16) % C::CW;
+            mma_ss(tS, sdesc_add(qd, ch * C::BM * C::ROWB + within * 2),
+                   sdesc_add(kd, ch * rows * C::ROWB + within * 2), id_s, ks > 0 ? 1u : 0u);
+          }
+          mma_commit(&bar_s[g & 1]);
+          if (t == n - 1) mma_commit(&bar_q_empty[qb]);  // last read of this Q buffer
         }
-        mma_commit(&bar_s[s_g & 1]);
-        if (s_t == s_n - 1) mma_commit(&bar_q_empty[qb]);  // last read of this Q buffer
-        ++s_g;
-        if (++s_t == s_n) {
-          s_t = 0;
-          ++s_qi;
-          s_it += gridDim.x;
-          s_more = next_item(s_it, s_sc, s_n);
-        }
-        return true;
-      };
-      if (s_more) ok = issue_s();
-      while (ok && v_more) {
-        // S one segment ahead: its S buffer was released by the softmax of segment v_g - 1,
-        // whose P barrier was waited for in the previous iteration.
-        if (s_more && !(ok = issue_s())) break;
-        if (!(ok = mbar_wait(&bar_p[v_g & 1], (v_g >> 1) & 1, &abort_sh))) break;
-        // the previous item's epilogue must have read O before the first PV overwrites it
-        if (v_t == 0 && v_qi > 0 && !(ok = mbar_wait(&bar_o_free, (v_qi - 1) & 1, &abort_sh))) break;
-        tc_fence_after();
-        int key0, rows;
-        v_sc.seg(v_t, &key0, &rows);
-        const int st = v_g % C::NST;
-        const uint64_t vd = sdesc(saddr(KVs + st * 2 * C::KV_BYTES + C::KV_BYTES), rows * C::ROWB, 8 * C::ROWB, C::SWZ);
-        const uint32_t tP = tmem + C::P_COL + (v_g & 1) * 32;
-        for (int ks = 0; ks < rows / 16; ++ks) {
-          const uint64_t bd = sdesc_add(vd, ks * 16 * C::ROWB);
-          mma_ts(tmem + C::O_COL, tP + ks * 8, bd, id_o, (v_t > 0 || ks > 0) ? 1u : 0u);
-        }
-        mma_commit(&bar_empty[st]);
-        mma_commit(&bar_pv);
-        ++v_g;
-        if (++v_t == v_n) {
-          mma_commit(&bar_o_full);
-          v_t = 0;
-          ++v_qi;
-          v_it += gridDim.x;
-          v_more = next_item(v_it, v_sc, v_n);
-        }
+        ++qi;
       }
       if (!ok) {
         abort_sh = 1;
         record_error(err, 1);
       }
     }
-  } else {
+  } else if (warp == 6) {
+    // ------------------------------------------------------------------ MMA issuer: O += P V
+    if (lane == 0 && !dead) {
+      constexpr uint32_t id_o = idesc_f16(128, D, kBf16, false, true);
+      int qi = 0, g = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        int b, h, qt;
+        decode_item(it, Hq, n_qt, &b, &h, &qt);
+        const FwdSched sc = fwd_schedule(qt * C::BM, L, W, S, p.sink_box);
+        const int n = sc.n();
+        if (n == 0) continue;
+        for (int t = 0; t < n; ++t, ++g) {
+          if (!(ok = mbar_wait(&bar_p[g & 1], (g >> 1) & 1, &abort_sh))) break;
+          // the previous item's epilogue must have read O before the first PV overwrites it
+          if (t == 0 && qi > 0 && !(ok = mbar_wait(&bar_o_free, (qi - 1) & 1, &abort_sh))) break;
+          tc_fence_after();
+          int key0, rows;
+          sc.seg(t, &key0, &rows);
+          const int st = g % C::NST;
+          const uint64_t vd = sdesc(saddr(KVs + st * 2 * C::KV_BYTES + C::KV_BYTES), rows * C::ROWB,
+                                    8 * C::ROWB, C::SWZ);
+          const uint32_t tP = tmem + C::P_COL + (g & 1) * 32;
+          for (int ks = 0; ks < rows / 16; ++ks)
+            mma_ts(tmem + C::O_COL, tP + ks * 8, sdesc_add(vd, ks * 16 * C::ROWB), id_o, (t > 0 || ks > 0) ? 1u : 0u);
+          mma_commit(&bar_empty[st]);
+          mma_commit(&bar_pv[g & 1]);
+          if (t == n - 1) mma_commit(&bar_o_full);
+        }
+        ++qi;
+      }
+      if (!ok) {
+        abort_sh = 1;
+        record_error(err, 1);
+      }
+    }
+  } else if (warp >= 2 && warp <= 5) {
     // ------------------------------------------------------------------ softmax (warps 2..5)
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
@@ -364,6 +357,8 @@ __global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
         sc.seg(t, &key0, &rows);
         const uint32_t tS = tmem + C::S_COL + (g & 1) * 64 + lane_off;
         const uint32_t tP = tmem + C::P_COL + (g & 1) * 32 + lane_off;
+        // P buffer g&1 is free once the PV of segment g - 2 has completed
+        if (g >= 2 && !(ok = mbar_wait(&bar_pv[g & 1], ((g - 2) >> 1) & 1, &abort_sh))) break;
         if (block_none_visible(r0w, r0w + 32, key0, key0 + rows, W, S, L)) {
           // nothing visible to this warp's rows: P = 0
           const uint32_t z[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
@@ -384,7 +379,7 @@ __global__ void __launch_bounds__(192, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
           if (__any_sync(0xffffffffu, rescale)) {
             // O must hold every PV issued so far: wait for the PV of segment g - 1 (t > 0 here,
             // since a first segment never rescales).
-            if (!(ok = mbar_wait(&bar_pv, (g - 1) & 1, &abort_sh))) break;
+            if (!(ok = mbar_wait(&bar_pv[(g - 1) & 1], ((g - 1) >> 1) & 1, &abort_sh))) break;
             tc_fence_after();
 #pragma unroll
             for (int c0 = 0; c0 < D; c0 += 16) {
@@ -469,9 +464,9 @@ cudaError_t launch_fwd_tc(const FwdParams& p0, cudaStream_t st, int* err) {
   e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e != cudaSuccess) return e;
   const int n_items = p.B * p.Hq * ((p.L + C::BM - 1) / C::BM);
-  const int grid = persistent_grid(kern, 192, C::SMEM, C::TMEM_COLS, n_items);
+  const int grid = persistent_grid(kern, 224, C::SMEM, C::TMEM_COLS, n_items);
   if (grid <= 0) return cudaErrorInvalidConfiguration;
-  kern<<<grid, 192, C::SMEM, st>>>(tm, p, err);
+  kern<<<grid, 224, C::SMEM, st>>>(tm, p, err);
   return cudaGetLastError();
 }
 
