@@ -18,11 +18,12 @@
 // (the reference loops over all L keys).  LSE and Delta rows come from the padded
 // [B, Hq, round_up(L, 64)] buffers (+inf / 0 past L), so padded query rows contribute zero.
 //
-// Warp roles (20 warps, 640 threads): warp 0 TMA producer, warp 1 issues the S / dP MMAs and
+// Warp roles (24 warps, 768 threads): warp 0 TMA producer, warp 1 issues the S / dP MMAs and
 // warp 2 the dQ MMAs (one thread each; a buffer-release barrier orders them),
-// warps 4..19 elementwise + epilogue: four warps per TMEM lane quadrant, 16 key columns each,
-// so that every scheduler has four independent elementwise warps to hide the TMEM and
-// special-function latencies.  Every mbarrier wait is bounded.
+// warps 4..19 elementwise: four warps per TMEM lane quadrant, 16 key columns each, so that
+// every scheduler has four independent elementwise warps to hide the TMEM and special-
+// function latencies; warps 20..23 epilogue: dQ is double-buffered in TMEM, so writing back
+// one item overlaps the next item's segments.  Every mbarrier wait is bounded.
 #include <type_traits>
 
 #include "sm100.cuh"
@@ -59,15 +60,16 @@ struct DqCfg {
   static constexpr int SMEM = 1024 + NQB * ITEM + NST * 2 * KV_BYTES;
   // dS of a segment overwrites its S columns: key columns [16k, 16k+16) of S hold, after the
   // elementwise pass, dS keys 16k..16k+15 in [16k, 16k+8) (the A operand of MMA K-step k).
-  static constexpr int S_COL = 0, DP_COL = 64 * NB, DQ_COL = 128 * NB;
-  static constexpr uint32_t TMEM_COLS = (128 * NB + D) <= 256 ? 256 : 512;
+  static constexpr int S_COL = 0, DP_COL = 64 * NB, DQ_COL = 128 * NB;  // dQ: 2 buffers of D
+  static constexpr uint32_t TMEM_COLS = 512;
   static constexpr int NGRP = SWA_DQ_NGRP;  // elementwise column groups
   static constexpr int CPG = 64 / NGRP;      // key columns per group
-  static constexpr int THREADS = 128 + 128 * NGRP;
+  static constexpr int EPI_WARP = 4 + 4 * NGRP;   // first of the four epilogue warps
+  static constexpr int THREADS = 128 + 128 * NGRP + 128;
 };
 
 template <typename T, int D>
-__global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(const __grid_constant__ DqTmaps tm,
+__global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(const __grid_constant__ DqTmaps tm,
                                                            const BwdParams p, int* err) {
   using C = DqCfg<D>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -79,7 +81,7 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
 
   __shared__ uint64_t bar_q_full[C::NQB], bar_q_empty[C::NQB];
   __shared__ uint64_t bar_full[C::NST], bar_empty[C::NST];
-  __shared__ uint64_t bar_s[C::NB], bar_p[C::NB], bar_rel[C::NB], bar_acc, bar_acc_free;
+  __shared__ uint64_t bar_s[C::NB], bar_p[C::NB], bar_rel[C::NB], bar_acc[2], bar_acc_free[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
 
@@ -105,8 +107,10 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
       mbar_init(&bar_s[s], 1);
       mbar_init(&bar_p[s], 128 * C::NGRP);
     }
-    mbar_init(&bar_acc, 1);
-    mbar_init(&bar_acc_free, 128 * C::NGRP);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar_acc[s], 1);
+      mbar_init(&bar_acc_free[s], 128);
+    }
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -236,21 +240,22 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
           const int gu = gs + u;
           const int bb = gu % C::NB, st = gu % C::NST;
           if (!(ok = mbar_wait(&bar_p[bb], (gu / C::NB) & 1, &abort_sh))) break;
-          // the previous item's epilogue must have read dQ before it is overwritten
-          if (u == 0 && qi > 0 && !(ok = mbar_wait(&bar_acc_free, (qi - 1) & 1, &abort_sh))) break;
+          // dQ buffer qi&1: the epilogue of item qi - 2 must have read it
+          if (u == 0 && qi >= 2 && !(ok = mbar_wait(&bar_acc_free[qi & 1], ((qi - 2) >> 1) & 1, &abort_sh))) break;
           tc_fence_after();
           int key0, rows;
           sc.seg(u, &key0, &rows);
           const uint64_t kmn = sdesc(saddr(KVs + st * 2 * C::KV_BYTES), rows * C::ROWB, 8 * C::ROWB, C::SWZ);
           for (int ks = 0; ks < rows / 16; ++ks) {
             const uint64_t bk = sdesc_add(kmn, ks * 16 * C::ROWB);
-            mma_ts(tmem + C::DQ_COL, tmem + C::S_COL + bb * 64 + ks * 16, bk, id_q, (u > 0 || ks > 0) ? 1u : 0u);
+            mma_ts(tmem + C::DQ_COL + (qi & 1) * D, tmem + C::S_COL + bb * 64 + ks * 16, bk, id_q,
+                   (u > 0 || ks > 0) ? 1u : 0u);
           }
           mma_commit(&bar_empty[st]);
           mma_commit(&bar_rel[bb]);
         }
         if (!ok) break;
-        mma_commit(&bar_acc);
+        mma_commit(&bar_acc[qi & 1]);
         // Q / dO are free (the S / dP MMAs finished before the elementwise pass, which came
         // before this item's last P barrier), and so are LSE / Delta (read by the elementwise
         // warps before their first P barrier of the item)
@@ -263,8 +268,59 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
         record_error(err, 1);
       }
     }
+  } else if (warp >= C::EPI_WARP) {
+    // ------------------------------------------------------------------ epilogue (4 warps)
+    // dQ * scale of one query row per thread, from the TMEM buffer of the item's parity, while
+    // the elementwise warps already work on the next item.
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    int qi = 0;
+    bool ok = !dead;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+      int b, h, qt;
+      decode_item(it, Hq, n_qt, &b, &h, &qt);
+      const int i = qt * C::BM + r;
+      const int n = ok ? fwd_schedule(qt * C::BM, L, W, S, p.sink_box).n() : 0;
+      const bool have = n > 0;
+      if (have) {
+        ok = mbar_wait(&bar_acc[qi & 1], (qi >> 1) & 1, &abort_sh);
+        tc_fence_after();
+      }
+      T* dqr = static_cast<T*>(p.dq) + b * p.sdq.b + h * p.sdq.h + (int64_t)i * p.sdq.l;
+      const uint32_t tq = tmem + C::DQ_COL + (qi & 1) * D + lane_off;
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 16) {
+        uint32_t a[16];
+        if (have && ok) {
+          tmem_ld16(tq + c0, a);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) a[e] = 0u;
+        }
+        if (i < L) {
+          uint32_t w[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            w[e] = Pack<T>::pack(__uint_as_float(a[2 * e]) * p.scale, __uint_as_float(a[2 * e + 1]) * p.scale);
+          uint4* dst = reinterpret_cast<uint4*>(dqr + c0);
+          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+      }
+      if (have) {
+        tc_fence_before();
+        mbar_arrive(&bar_acc_free[qi & 1]);
+        ++qi;
+      }
+    }
+    if (!ok && !dead) {
+      abort_sh = 1;
+      record_error(err, 1);
+    }
   } else if (warp >= 4) {
-    // ------------------------------------------------------------------ elementwise + epilogue
+    // ------------------------------------------------------------------ elementwise
     const int quad = warp & 3, grp = (warp - 4) >> 2;
     constexpr int CPG = C::CPG;
     const int r = quad * 32 + lane;  // query row of the tile (TMEM lane)
@@ -337,37 +393,7 @@ __global__ void __launch_bounds__(128 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
         tc_fence_before();
         mbar_arrive(&bar_p[bb]);
       }
-      // ---- epilogue: dQ * scale of row i, 8-column chunks dealt round-robin to the groups
-      const bool have = n > 0 && ok;
-      if (have) {
-        ok = mbar_wait(&bar_acc, qi & 1, &abort_sh);
-        tc_fence_after();
-      }
-      T* dqr = static_cast<T*>(p.dq) + b * p.sdq.b + h * p.sdq.h + (int64_t)i * p.sdq.l;
-#pragma unroll
-      for (int c0 = grp * 8; c0 < D; c0 += 8 * C::NGRP) {
-        uint32_t a[8];
-        if (have && ok) {
-          asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                       : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]),
-                         "=r"(a[7])
-                       : "r"(tmem + C::DQ_COL + c0 + lane_off));
-          tmem_ld_wait();
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) a[e] = 0u;
-        }
-        if (i < L) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            w[e] = Pack<T>::pack(__uint_as_float(a[2 * e]) * p.scale, __uint_as_float(a[2 * e + 1]) * p.scale);
-          *reinterpret_cast<uint4*>(dqr + c0) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      }
-      if (have) {
-        tc_fence_before();
-        mbar_arrive(&bar_acc_free);
+      if (n > 0 && ok) {
         gs += n;
         ++qi;
       }
