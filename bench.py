@@ -65,7 +65,8 @@ def kernel_work(w: wl.Workload, batch: int):
         "fwd": dict(flops=4 * d * pairs, bytes=qbytes + 2 * kbytes + qbytes + rows),
         "bwd_preprocess": dict(flops=2 * qbytes // e, bytes=2 * qbytes + rows),
         "bwd_dkdv": dict(flops=8 * d * pairs, bytes=2 * qbytes + 2 * kbytes + 2 * rows + 2 * kbytes),
-        "bwd_dq": dict(flops=6 * d * pairs, bytes=2 * qbytes + 2 * kbytes + 2 * rows + qbytes),
+        # dQ pass: Q, dO, O, K, V, LSE read; dQ and Delta written
+        "bwd_dq": dict(flops=6 * d * pairs, bytes=3 * qbytes + 2 * kbytes + 2 * rows + qbytes),
     }
 
 
@@ -178,8 +179,8 @@ def device_timed(w, dev, rank, steps, warmup):
     q, k, v, do = wl.make_inputs(w, device=dev)
     plan = plan_mod.SwaPlan(q, k, v, w.window_size, w.sink_size, None, dout=do)
     stream = torch.cuda.current_stream(dev)
-    phases = ("fwd", "bwd_preprocess", "bwd_dkdv", "bwd_dq")
-    fns = (plan.fwd, plan.bwd_preprocess, plan.bwd_dkdv, plan.bwd_dq)
+    phases = ("fwd", "bwd_dq", "bwd_dkdv")
+    fns = (plan.fwd, plan.bwd_dq, plan.bwd_dkdv)
     for _ in range(warmup):
         plan.step(stream)
     torch.cuda.synchronize(dev)

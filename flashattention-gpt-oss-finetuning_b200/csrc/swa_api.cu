@@ -261,9 +261,9 @@ int swa_bwd(const SwaBwdArgs* a, void* stream) {
   int st = build_bwd(a, &kp);
   if (st || (int64_t)a->p.batch * a->p.seq_len == 0) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if ((st = dispatch<Pre>(a->p, kp, s))) return st;
-  if ((st = dispatch<Dkdv>(a->p, kp, s))) return st;
-  return dispatch<Dq>(a->p, kp, s);
+  // the dQ pass also computes Delta = rowsum(dO * O) into the workspace for the dK/dV pass
+  if ((st = dispatch<Dq>(a->p, kp, s))) return st;
+  return dispatch<Dkdv>(a->p, kp, s);
 }
 
 }  // extern "C"

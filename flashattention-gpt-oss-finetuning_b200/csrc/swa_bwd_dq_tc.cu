@@ -35,7 +35,7 @@ namespace swa {
 using namespace sm100;
 
 struct DqTmaps {
-  CUtensorMap q, dout, k, v, ks, vs, lse, delta;
+  CUtensorMap q, dout, o, k, v, ks, vs, lse;
 };
 
 template <int D>
@@ -46,7 +46,8 @@ struct DqCfg {
   static constexpr int ROWB = CW * 2;
   static constexpr uint32_t SWZ = CW == 64 ? kSw128 : (CW == 32 ? kSw64 : kSw32);
   static constexpr int QT_BYTES = BM * D * 2;        // Q or dO tile
-  static constexpr int ITEM = 2 * QT_BYTES + 1024;   // Q, dO, LSE[128], Delta[128]
+  static constexpr int ITEM = 3 * QT_BYTES + 1024;   // Q, dO, LSE[128], Delta[128], O
+  static constexpr int O_OFF = 2 * QT_BYTES + 1024;
 #ifndef SWA_DQ_NB
 #define SWA_DQ_NB 3
 #endif
@@ -56,7 +57,7 @@ struct DqCfg {
   static constexpr int NB = D <= 64 ? SWA_DQ_NB : 2;  // TMEM buffers of S (and dS) and dP
   static constexpr int NQB = D <= 64 ? 2 : 1;        // item buffers
   static constexpr int KV_BYTES = BN * D * 2;        // one K or V segment
-  static constexpr int NST = D <= 64 ? 8 : 4;        // K/V stages
+  static constexpr int NST = D <= 64 ? 6 : 3;        // K/V stages
   static constexpr int SMEM = 1024 + NQB * ITEM + NST * 2 * KV_BYTES;
   // dS of a segment overwrites its S columns: key columns [16k, 16k+16) of S hold, after the
   // elementwise pass, dS keys 16k..16k+15 in [16k, 16k+8) (the A operand of MMA K-step k).
@@ -79,7 +80,7 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
   unsigned char* ITs = smem;                     // [NQB][Q, dO, lse, delta]
   unsigned char* KVs = smem + C::NQB * C::ITEM;  // [NST][K, V]
 
-  __shared__ uint64_t bar_q_full[C::NQB], bar_q_empty[C::NQB];
+  __shared__ uint64_t bar_q_full[C::NQB], bar_q_empty[C::NQB], bar_dready[C::NQB];
   __shared__ uint64_t bar_full[C::NST], bar_empty[C::NST];
   __shared__ uint64_t bar_s[C::NB], bar_p[C::NB], bar_rel[C::NB], bar_acc[2], bar_acc_free[2];
   __shared__ uint32_t tmem_base_sh;
@@ -96,6 +97,7 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
     abort_sh = dead ? 1 : 0;
     for (int s = 0; s < C::NQB; ++s) {
       mbar_init(&bar_q_full[s], 1);
+      mbar_init(&bar_dready[s], 128);
       mbar_init(&bar_q_empty[s], 1);
     }
     for (int s = 0; s < C::NST; ++s) {
@@ -143,17 +145,16 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
         if (qi >= C::NQB && !(ok = mbar_wait(&bar_q_empty[qb], ((qi / C::NQB) - 1) & 1, &abort_sh))) break;
         unsigned char* Ib = ITs + qb * C::ITEM;
         const int row = b * Hq + h;
-        mbar_arrive_expect_tx(&bar_q_full[qb], 2 * C::QT_BYTES + 1024);
+        mbar_arrive_expect_tx(&bar_q_full[qb], 3 * C::QT_BYTES + 512);
 #pragma unroll
         for (int c = 0; c < C::NCH; ++c) {
           tma_load_4d(Ib + c * C::BM * C::ROWB, &tm.q, &bar_q_full[qb], c * C::CW, q0, h, b);
           tma_load_4d(Ib + C::QT_BYTES + c * C::BM * C::ROWB, &tm.dout, &bar_q_full[qb], c * C::CW, q0, h, b);
+          tma_load_4d(Ib + C::O_OFF + c * C::BM * C::ROWB, &tm.o, &bar_q_full[qb], c * C::CW, q0, h, b);
         }
-        // LSE / Delta rows are padded to a multiple of 64 (+inf / 0)
-        for (int k = 0; k < 2; ++k) {
+        // LSE rows are padded to a multiple of 64 (+inf)
+        for (int k = 0; k < 2; ++k)
           tma_load_2d(Ib + 2 * C::QT_BYTES + k * 256, &tm.lse, &bar_q_full[qb], q0 + 64 * k, row);
-          tma_load_2d(Ib + 2 * C::QT_BYTES + 512 + k * 256, &tm.delta, &bar_q_full[qb], q0 + 64 * k, row);
-        }
         for (int t = 0; t < n; ++t, ++gs) {
           const int st = gs % C::NST;
           if (gs >= C::NST && !(ok = mbar_wait(&bar_empty[st], ((gs / C::NST) - 1) & 1, &abort_sh))) break;
@@ -270,22 +271,64 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
     }
   } else if (warp >= C::EPI_WARP) {
     // ------------------------------------------------------------------ epilogue (4 warps)
-    // dQ * scale of one query row per thread, from the TMEM buffer of the item's parity, while
-    // the elementwise warps already work on the next item.
+    // Per item: Delta = rowsum(dO * O) of the NEXT item (from its staged dO and O tiles; into
+    // shared memory for the elementwise warps and to the workspace for the dK/dV pass), then
+    // dQ * scale of this item from the TMEM buffer of its parity.  One query row per thread.
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    int qi = 0;
+    constexpr uint32_t SWM = C::ROWB / 16 - 1;  // swizzle: 16-byte unit ^= (offset >> 7) & SWM
+    int qi = 0, dqi = 0, it_d = blockIdx.x;
     bool ok = !dead;
+    // Delta of the next item with segments; false when there is none
+    auto delta_next = [&]() -> bool {
+      for (; it_d < n_items; it_d += gridDim.x) {
+        int b, h, qt;
+        decode_item(it_d, Hq, n_qt, &b, &h, &qt);
+        if (fwd_schedule(qt * C::BM, L, W, S, p.sink_box).n() == 0) continue;
+        const int qb = dqi % C::NQB;
+        if (ok) ok = mbar_wait(&bar_q_full[qb], (dqi / C::NQB) & 1, &abort_sh);
+        float acc = 0.f;
+        if (ok) {
+          unsigned char* Ib = ITs + qb * C::ITEM;
+#pragma unroll
+          for (int ch = 0; ch < C::NCH; ++ch) {
+#pragma unroll
+            for (int u = 0; u < C::ROWB / 16; ++u) {
+              uint32_t off = r * C::ROWB + u * 16;
+              off ^= ((off >> 7) & SWM) << 4;
+              const uint4 dv = *reinterpret_cast<const uint4*>(Ib + C::QT_BYTES + ch * C::BM * C::ROWB + off);
+              const uint4 ov = *reinterpret_cast<const uint4*>(Ib + C::O_OFF + ch * C::BM * C::ROWB + off);
+              const T* de = reinterpret_cast<const T*>(&dv);
+              const T* oe = reinterpret_cast<const T*>(&ov);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) acc = fmaf(Pack<T>::to(de[e]), Pack<T>::to(oe[e]), acc);
+            }
+          }
+          reinterpret_cast<float*>(Ib + 2 * C::QT_BYTES + 512)[r] = acc;
+        }
+        const int i = qt * C::BM + r;
+        if (i < p.lse_ld) p.delta[((int64_t)b * Hq + h) * p.lse_ld + i] = (i < L) ? acc : 0.f;
+        mbar_arrive(&bar_dready[qb]);
+        ++dqi;
+        it_d += gridDim.x;
+        return true;
+      }
+      return false;
+    };
+    delta_next();
     for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
       int b, h, qt;
       decode_item(it, Hq, n_qt, &b, &h, &qt);
       const int i = qt * C::BM + r;
-      const int n = ok ? fwd_schedule(qt * C::BM, L, W, S, p.sink_box).n() : 0;
+      const int n = fwd_schedule(qt * C::BM, L, W, S, p.sink_box).n();
       const bool have = n > 0;
       if (have) {
-        ok = mbar_wait(&bar_acc[qi & 1], (qi >> 1) & 1, &abort_sh);
+        delta_next();  // the following item's Delta overlaps this item's last segments
+        if (ok) ok = mbar_wait(&bar_acc[qi & 1], (qi >> 1) & 1, &abort_sh);
         tc_fence_after();
+      } else if (i < p.lse_ld) {
+        p.delta[((int64_t)b * Hq + h) * p.lse_ld + i] = 0.f;  // no key visible: Delta unused
       }
       T* dqr = static_cast<T*>(p.dq) + b * p.sdq.b + h * p.sdq.h + (int64_t)i * p.sdq.l;
       const uint32_t tq = tmem + C::DQ_COL + (qi & 1) * D + lane_off;
@@ -338,7 +381,7 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
       const int n = ok ? sc.n() : 0;
       float lse_r = 0.f, dl_r = 0.f;
       if (n > 0) {
-        if (!(ok = mbar_wait(&bar_q_full[qi % C::NQB], (qi / C::NQB) & 1, &abort_sh))) break;
+        if (!(ok = mbar_wait(&bar_dready[qi % C::NQB], (qi / C::NQB) & 1, &abort_sh))) break;
         const float* st_rows = reinterpret_cast<const float*>(ITs + (qi % C::NQB) * C::ITEM + 2 * C::QT_BYTES);
         lse_r = st_rows[r];
         dl_r = st_rows[128 + r];
@@ -423,8 +466,8 @@ cudaError_t launch_bwd_dq_tc(const BwdParams& p0, cudaStream_t st, int* err) {
             make_tmap_bhld(&tm.v, p.v, p.B, p.Hkv, p.L, D, p.sv.b, p.sv.h, p.sv.l, C::CW, C::BN) &&
             make_tmap_bhld(&tm.ks, p.k, p.B, p.Hkv, p.L, D, p.sk.b, p.sk.h, p.sk.l, C::CW, sb) &&
             make_tmap_bhld(&tm.vs, p.v, p.B, p.Hkv, p.L, D, p.sv.b, p.sv.h, p.sv.l, C::CW, sb) &&
-            make_tmap_rows_f32(&tm.lse, p.lse, (long long)p.B * p.Hq, p.lse_ld, p.lse_ld, 64) &&
-            make_tmap_rows_f32(&tm.delta, p.delta, (long long)p.B * p.Hq, p.lse_ld, p.lse_ld, 64);
+            make_tmap_bhld(&tm.o, p.o, p.B, p.Hq, p.L, D, p.so.b, p.so.h, p.so.l, C::CW, C::BM) &&
+            make_tmap_rows_f32(&tm.lse, p.lse, (long long)p.B * p.Hq, p.lse_ld, p.lse_ld, 64);
   if (!ok) return cudaErrorInvalidValue;
   auto kern = bwd_dq_tc_kernel<T, D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);

@@ -74,9 +74,9 @@ class SwaPlan:
         self.launches += 1
 
     def bwd(self, stream=None):
-        self.bwd_preprocess(stream)
-        self.bwd_dkdv(stream)
+        """dQ (which also writes Delta to the workspace), then dK / dV."""
         self.bwd_dq(stream)
+        self.bwd_dkdv(stream)
 
     def step(self, stream=None):
         """One forward + backward over the bound buffers."""

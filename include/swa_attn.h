@@ -101,19 +101,21 @@ SWA_API int swa_fwd(const SwaFwdArgs* args, void* stream);
 /* Scratch the backward needs (Delta rows and the sink-key partial sums), in bytes. */
 SWA_API size_t swa_bwd_workspace_size(const SwaProblem* p);
 
-/* Full backward: preprocess + dK/dV + dQ.  Replaces flash_attention_gpt_oss.py:397-435. */
+/* Full backward: dQ (which also writes Delta) then dK/dV.  Replaces
+ * flash_attention_gpt_oss.py:397-435. */
 SWA_API int swa_bwd(const SwaBwdArgs* args, void* stream);
 
-/* Delta[b,h,i] = sum_d dout * o, written to the front of the workspace.
- * Replaces flash_attention_gpt_oss.py:403. */
+/* Delta[b,h,i] = sum_d dout * o, written to the front of the workspace (stand-alone; swa_bwd
+ * and swa_bwd_dq compute it inside the dQ pass).  Replaces flash_attention_gpt_oss.py:403. */
 SWA_API int swa_bwd_preprocess(const SwaBwdArgs* args, void* stream);
 
-/* dq; needs swa_bwd_preprocess to have run on the same workspace.
- * Replaces flash_attention_gpt_oss.py:306-321, 334-338. */
+/* dq; also computes Delta = rowsum(dout * o) and writes it to the workspace, where
+ * swa_bwd_dkdv reads it.  Replaces flash_attention_gpt_oss.py:306-321, 334-338, 403. */
 SWA_API int swa_bwd_dq(const SwaBwdArgs* args, void* stream);
 
-/* dk, dv, deterministic (each KV tile owned by one CTA, GQA group looped inside);
- * needs swa_bwd_preprocess.  Replaces flash_attention_gpt_oss.py:295-304, 323-332. */
+/* dk, dv, deterministic (each KV tile owned by one CTA, GQA group looped inside); needs
+ * Delta in the workspace (from swa_bwd_dq or swa_bwd_preprocess).  Replaces
+ * flash_attention_gpt_oss.py:295-304, 323-332. */
 SWA_API int swa_bwd_dkdv(const SwaBwdArgs* args, void* stream);
 
 /* Backward that allocates nothing and takes no workspace.  No counterpart in the reference.
