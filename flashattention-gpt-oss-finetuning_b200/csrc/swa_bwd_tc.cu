@@ -62,7 +62,13 @@ struct DkdvCfg {
   static constexpr int DK_COL = 128 * NB, DV_COL = 128 * NB + D;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr int NGRP = 4;        // elementwise column groups
-  static constexpr int CPG = 64 / NGRP;  // query columns per group
+#ifndef SWA_DKDV_STEP_SETS
+#define SWA_DKDV_STEP_SETS 2
+#endif
+  static constexpr int STEP_SETS = SWA_DKDV_STEP_SETS;  // steps in flight in the elementwise warps
+  // A step set waits on TMEM buffer gt % NB with the parity of gt / NB; its previous step
+  // (gt - STEP_SETS) must imply that step gt - NB has completed, or the parity could alias.
+  static_assert(STEP_SETS <= NB, "more elementwise step sets than S^T buffers");
   static constexpr int THREADS = 128 + 128 * NGRP;
 };
 
@@ -144,7 +150,7 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
     for (int s = 0; s < C::NB; ++s) {
       mbar_init(&bar_rel[s], 1);
       mbar_init(&bar_s[s], 1);
-      mbar_init(&bar_p[s], 128 * C::NGRP);
+      mbar_init(&bar_p[s], 128 * C::NGRP / C::STEP_SETS);
     }
     mbar_init(&bar_acc, 1);
     mbar_init(&bar_acc_free, 128 * C::NGRP);
@@ -298,7 +304,11 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ elementwise + epilogue
     const int quad = warp & 3, grp = (warp - 4) >> 2;
-    constexpr int CPG = C::CPG;
+    // The column groups form STEP_SETS sets; set k takes the steps with global index
+    // gt % STEP_SETS == k, so consecutive steps are processed concurrently.
+    constexpr int SCOLS = 64 * C::STEP_SETS / C::NGRP;  // query columns per warp per step
+    const int sub = grp % C::STEP_SETS;
+    const int scol0 = (grp / C::STEP_SETS) * SCOLS;
     const int r = quad * 32 + lane;  // key row of the tile (TMEM lane)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float sl2 = p.scale_log2;
@@ -312,45 +322,51 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
       const int kw0 = k0 + quad * 32;  // this warp's 32 keys
       for (int t = 0; t < itm.n && ok; ++t) {
         const int gt = gs + t;
+        if (gt % C::STEP_SETS != sub) continue;  // another step set takes this step
         const int bb = gt % C::NB, st = gt % C::NST;
         if (!(ok = mbar_wait(&bar_s[bb], (gt / C::NB) & 1, &abort_sh))) break;
         tc_fence_after();
         const int it = itm.it0 + t;
-        const int qc0 = (itm.qt_lo + it % itm.n_qtr) * 64 + grp * CPG;  // first query column
-        const uint32_t tP = tmem + C::S_COL + bb * 64 + grp * CPG + lane_off;  // over this group's S^T
-        const uint32_t tdS = tP + CPG / 2;
-        if (block_none_visible(qc0, qc0 + CPG, kw0, kw0 + 32, W, S, L)) {
-          const uint32_t z[8] = {0u};
-          tmem_st8(tP, z);
-          tmem_st8(tdS, z);
-        } else {
-          const bool full = block_all_visible(qc0, qc0 + CPG, kw0, kw0 + 32, W, S, L);
-          float s[CPG], dp[CPG];
-          tmem_ld16(tmem + C::S_COL + bb * 64 + grp * CPG + lane_off, reinterpret_cast<uint32_t*>(s));
-          tmem_ld16(tmem + C::DP_COL + bb * 64 + grp * CPG + lane_off, reinterpret_cast<uint32_t*>(dp));
-          const float* lse_s = reinterpret_cast<const float*>(STs + st * C::STAGE + 2 * C::QT_BYTES) + grp * CPG;
-          const float* dl_s = lse_s + 64;
-          tmem_ld_wait();
-          // query i = qc0 + c sees key j iff c >= c_min and (c < c_max or j < S)
-          const int c_min = j - qc0;
-          const int c_max = (W > 0 && j >= S) ? j + W - qc0 : (j < S ? 1 << 30 : -(1 << 30));
-          uint32_t pw[CPG / 2], dw[CPG / 2];
+        const float* lse_base = reinterpret_cast<const float*>(STs + st * C::STAGE + 2 * C::QT_BYTES);
 #pragma unroll
-          for (int e = 0; e < CPG / 2; ++e) {
-            float pv[2], dv[2];
+        for (int ch = 0; ch < SCOLS / 16; ++ch) {
+          const int col = scol0 + ch * 16;  // first of this chunk's 16 query columns
+          const int qc0 = (itm.qt_lo + it % itm.n_qtr) * 64 + col;
+          const uint32_t tP = tmem + C::S_COL + bb * 64 + col + lane_off;  // over this chunk's S^T
+          const uint32_t tdS = tP + 8;
+          if (block_none_visible(qc0, qc0 + 16, kw0, kw0 + 32, W, S, L)) {
+            const uint32_t z[8] = {0u};
+            tmem_st8(tP, z);
+            tmem_st8(tdS, z);
+          } else {
+            const bool full = block_all_visible(qc0, qc0 + 16, kw0, kw0 + 32, W, S, L);
+            float s[16], dp[16];
+            tmem_ld16(tmem + C::S_COL + bb * 64 + col + lane_off, reinterpret_cast<uint32_t*>(s));
+            tmem_ld16(tmem + C::DP_COL + bb * 64 + col + lane_off, reinterpret_cast<uint32_t*>(dp));
+            const float* lse_s = lse_base + col;
+            const float* dl_s = lse_s + 64;
+            tmem_ld_wait();
+            // query i = qc0 + c sees key j iff c >= c_min and (c < c_max or j < S)
+            const int c_min = j - qc0;
+            const int c_max = (W > 0 && j >= S) ? j + W - qc0 : (j < S ? 1 << 30 : -(1 << 30));
+            uint32_t pw[8], dw[8];
 #pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
-              const int c = 2 * e + h2;
-              float pr = fast_exp2(fmaf(s[c], sl2, -lse_s[c]));
-              if (!full) pr = (c >= c_min && c < c_max) ? pr : 0.f;
-              pv[h2] = pr;
-              dv[h2] = pr * (dp[c] - dl_s[c]);
+            for (int e = 0; e < 8; ++e) {
+              float pv[2], dv[2];
+#pragma unroll
+              for (int h2 = 0; h2 < 2; ++h2) {
+                const int c = 2 * e + h2;
+                float pr = fast_exp2(fmaf(s[c], sl2, -lse_s[c]));
+                if (!full) pr = (c >= c_min && c < c_max) ? pr : 0.f;
+                pv[h2] = pr;
+                dv[h2] = pr * (dp[c] - dl_s[c]);
+              }
+              pw[e] = Pack<T>::pack(pv[0], pv[1]);
+              dw[e] = Pack<T>::pack(dv[0], dv[1]);
             }
-            pw[e] = Pack<T>::pack(pv[0], pv[1]);
-            dw[e] = Pack<T>::pack(dv[0], dv[1]);
+            tmem_st8(tP, pw);
+            tmem_st8(tdS, dw);
           }
-          tmem_st8(tP, pw);
-          tmem_st8(tdS, dw);
         }
         tmem_st_wait();
         tc_fence_before();
