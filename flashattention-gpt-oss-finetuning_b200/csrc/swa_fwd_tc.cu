@@ -39,6 +39,7 @@ using namespace sm100;
 
 struct FwdTmaps {
   CUtensorMap q, k, v, ks, vs;  // ks / vs: same tensors as k / v with an SB-row box
+  CUtensorMap o;                // output, 128-row box (TMA store of the staged O tile)
 };
 
 template <int D>
@@ -50,7 +51,7 @@ struct FwdCfg {
   static constexpr uint32_t SWZ = CW == 64 ? kSw128 : (CW == 32 ? kSw64 : kSw32);
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;  // one K or V buffer
-  static constexpr int SMEM = 1024 + 2 * Q_BYTES + NST * 2 * KV_BYTES;
+  static constexpr int SMEM = 1024 + 3 * Q_BYTES + NST * 2 * KV_BYTES;  // + O staging tile
   static constexpr uint32_t TMEM_COLS = (192 + D) <= 256 ? 256 : 512;
   static constexpr int S_COL = 0, P_COL = 128, O_COL = 192;
 };
@@ -166,6 +167,7 @@ __global__ void __launch_bounds__(224, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* Qs = smem;                    // [2][Q_BYTES]
   unsigned char* KVs = smem + 2 * C::Q_BYTES;  // stage s: K at s*2*KV_BYTES, V after it
+  unsigned char* Ost = KVs + C::NST * 2 * C::KV_BYTES;  // O staging tile (Q layout)
 
   __shared__ uint64_t bar_q_full[2], bar_q_empty[2];
   __shared__ uint64_t bar_full[C::NST], bar_empty[C::NST];
@@ -398,11 +400,14 @@ __global__ void __launch_bounds__(224, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
       }
       if (n > 0 && ok) ok = mbar_wait(&bar_o_full, qi & 1, &abort_sh);
       if (n > 0 && ok) tc_fence_after();
-      // ---- epilogue: O / l, base-2 LSE (a row that sees no key gets O = 0, LSE = -inf)
+      // ---- epilogue: O / l, base-2 LSE (a row that sees no key gets O = 0, LSE = -inf).
+      // O goes through the swizzled staging tile and one TMA store (rows past L are clipped).
       const bool have_o = n > 0 && ok;
       const float l = rs.l;
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      T* orow = static_cast<T*>(p.o) + b * p.so.b + h * p.so.h + (int64_t)i * p.so.l;
+      if (threadIdx.x == 64) bulk_wait_read_all();  // the previous item's store has read Ost
+      named_bar_sync(1, 128);
+      constexpr uint32_t SWM = C::ROWB / 16 - 1;
 #pragma unroll
       for (int c0 = 0; c0 < D; c0 += 16) {
         uint32_t o[16];
@@ -413,15 +418,25 @@ __global__ void __launch_bounds__(224, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
 #pragma unroll
           for (int e = 0; e < 16; ++e) o[e] = 0u;
         }
-        if (i < L) {
-          uint32_t w[8];
+        uint32_t w[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            w[e] = Pack<T>::pack(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
-          uint4* dst = reinterpret_cast<uint4*>(orow + c0);
-          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        for (int e = 0; e < 8; ++e)
+          w[e] = Pack<T>::pack(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+#pragma unroll
+        for (int hv = 0; hv < 2; ++hv) {
+          const int d0 = c0 + 8 * hv;  // 8 elements = one 16-byte unit
+          uint32_t off = r * C::ROWB + ((d0 % C::CW) / 8) * 16;
+          off ^= ((off >> 7) & SWM) << 4;
+          *reinterpret_cast<uint4*>(Ost + (d0 / C::CW) * C::BM * C::ROWB + off) =
+              make_uint4(w[4 * hv], w[4 * hv + 1], w[4 * hv + 2], w[4 * hv + 3]);
         }
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(1, 128);
+      if (threadIdx.x == 64) {
+#pragma unroll
+        for (int c = 0; c < C::NCH; ++c) tma_store_4d(&tm.o, Ost + c * C::BM * C::ROWB, c * C::CW, q0, h, b);
+        bulk_commit();
       }
       if (i < L)
         p.lse[((int64_t)b * Hq + h) * p.lse_ld + i] = l > 0.f ? rs.m_used + __log2f(l) : -INFINITY;
@@ -433,6 +448,7 @@ __global__ void __launch_bounds__(224, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
       }
       if (n > 0) ++qi;
     }
+    if (threadIdx.x == 64) bulk_wait_all();  // O stores complete before the CTA exits
     if (!ok) {
       abort_sh = 1;
       record_error(err, 1);
@@ -456,7 +472,8 @@ cudaError_t launch_fwd_tc(const FwdParams& p0, cudaStream_t st, int* err) {
             make_tmap_bhld(&tm.k, p.k, p.B, p.Hkv, p.L, D, p.sk.b, p.sk.h, p.sk.l, C::CW, C::BN) &&
             make_tmap_bhld(&tm.v, p.v, p.B, p.Hkv, p.L, D, p.sv.b, p.sv.h, p.sv.l, C::CW, C::BN) &&
             make_tmap_bhld(&tm.ks, p.k, p.B, p.Hkv, p.L, D, p.sk.b, p.sk.h, p.sk.l, C::CW, sb) &&
-            make_tmap_bhld(&tm.vs, p.v, p.B, p.Hkv, p.L, D, p.sv.b, p.sv.h, p.sv.l, C::CW, sb);
+            make_tmap_bhld(&tm.vs, p.v, p.B, p.Hkv, p.L, D, p.sv.b, p.sv.h, p.sv.l, C::CW, sb) &&
+            make_tmap_bhld(&tm.o, p.o, p.B, p.Hq, p.L, D, p.so.b, p.so.h, p.so.l, C::CW, C::BM);
   if (!ok) return cudaErrorInvalidValue;
   auto kern = fwd_tc_kernel<T, D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
