@@ -84,29 +84,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return mbar_wait_ns(bar, parity, abort, kWaitLimitNs);
 }
 
-// Shared-memory progress counters (monotone, so a waiter can never confuse two rounds the
-// way an mbarrier parity can when the producer runs more than one phase ahead).
-__device__ __forceinline__ void counter_publish(int* c, int v) {
-  asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(saddr(c)), "r"(v) : "memory");
-}
-__device__ __forceinline__ int counter_read(const int* c) {
-  int v;
-  asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(saddr(c)) : "memory");
-  return v;
-}
-// Bounded wait until *c >= target; false when the limit passes or `abort` is raised.
-__device__ __forceinline__ bool counter_wait(const int* c, int target, volatile int* abort) {
-  if (counter_read(c) >= target) return true;
-  const uint64_t t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (counter_read(c) >= target) return true;
-    if ((i & 255u) == 0) {
-      if (*abort) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) return false;
-    }
-  }
-}
-
 // ---------------------------------------------------------------------------------------
 // TMA (tiled, no multicast; every source is this GPU's own global memory)
 // ---------------------------------------------------------------------------------------

@@ -123,35 +123,18 @@ size_t delta_bytes(const SwaProblem& p) {
   return (n + 255) & ~(size_t)255;
 }
 
-// allow_fused: let the dQ pass carry the far sink pairs (the default; the no-alloc entry
-// point turns it off when the fused partials would not fit its static scratch).
-swa::SinkSplit split_of(const SwaProblem& p, bool allow_fused) {
+swa::SinkSplit split_of(const SwaProblem& p) {
   return swa::sink_split(p.seq_len, effective_window(p.window_size, p.seq_len), p.sink_size,
-                         p.n_q_heads / p.n_kv_heads, swa::kDkdvKeyTile, swa::kDkdvQueryTile, p.head_dim,
-                         allow_fused);
+                         p.n_q_heads / p.n_kv_heads, swa::kDkdvKeyTile, swa::kDkdvQueryTile);
 }
 
-size_t round256(size_t n) { return (n + 255) & ~(size_t)255; }
-
-// Near / far-chunk partials, then the fused far partials.
-size_t near_partial_bytes(const SwaProblem& p, bool allow_fused) {
-  const swa::SinkSplit ss = split_of(p, allow_fused);
-  return round256((size_t)swa::sink_partial_floats(ss, p.batch, p.n_kv_heads, p.head_dim) * sizeof(float));
+size_t partial_bytes(const SwaProblem& p) {
+  const swa::SinkSplit ss = split_of(p);
+  size_t n = (size_t)swa::sink_partial_floats(ss, p.batch, p.n_kv_heads, p.head_dim) * sizeof(float);
+  return (n + 255) & ~(size_t)255;
 }
 
-size_t partial_bytes(const SwaProblem& p, bool allow_fused) {
-  const swa::SinkSplit ss = split_of(p, allow_fused);
-  return near_partial_bytes(p, allow_fused) +
-         round256((size_t)swa::sink_fused_floats(ss, p.batch, p.n_kv_heads, p.n_q_heads / p.n_kv_heads,
-                                                 p.sink_size, p.head_dim) * sizeof(float));
-}
-
-size_t workspace_bytes(const SwaProblem& p, bool allow_fused) {
-  if (check_problem(p) != SWA_OK) return delta_bytes(p);
-  return delta_bytes(p) + partial_bytes(p, allow_fused);
-}
-
-int build_bwd(const SwaBwdArgs* a, swa::BwdParams* kp, bool allow_fused = true) {
+int build_bwd(const SwaBwdArgs* a, swa::BwdParams* kp) {
   if (!a) return SWA_ERR_INVALID_ARG;
   int st = check_problem(a->p);
   if (st) return st;
@@ -160,7 +143,7 @@ int build_bwd(const SwaBwdArgs* a, swa::BwdParams* kp, bool allow_fused = true) 
   for (const SwaTensor* t : need)
     if ((st = check_tensor(*t, !empty))) return st;
   if (!empty && !a->lse) return SWA_ERR_INVALID_ARG;
-  if (!empty && (!a->workspace || a->workspace_bytes < workspace_bytes(a->p, allow_fused)))
+  if (!empty && (!a->workspace || a->workspace_bytes < swa_bwd_workspace_size(&a->p)))
     return SWA_ERR_WORKSPACE;
   if (!empty && (reinterpret_cast<uintptr_t>(a->workspace) & 255u)) return SWA_ERR_WORKSPACE;
   const SwaProblem& p = a->p;
@@ -175,25 +158,11 @@ int build_bwd(const SwaBwdArgs* a, swa::BwdParams* kp, bool allow_fused = true) 
   kp->W = effective_window(p.window_size, p.seq_len); kp->S = p.sink_size;
   kp->scale = p.softmax_scale;
   kp->scale_log2 = p.softmax_scale * swa::kLog2e;
-  const swa::SinkSplit ss = split_of(p, allow_fused);
+  const swa::SinkSplit ss = split_of(p);
   kp->part = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + delta_bytes(p));
-  kp->partf = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + delta_bytes(p) +
-                                       near_partial_bytes(p, allow_fused));
   kp->nst = ss.nst; kp->sp = ss.sp; kp->nc = ss.nc; kp->ch = ss.ch;
   kp->bn_split = ss.bn; kp->bm_split = ss.bm;
-  kp->nf = ss.nf; kp->qf0 = ss.qf0; kp->rfar = ss.rfar;
   return SWA_OK;
-}
-
-// dQ (which also writes Delta and, fused, the far sink partials), then dK/dV and the
-// sink-row reduction.
-int run_bwd(const SwaBwdArgs* a, void* stream, bool allow_fused) {
-  swa::BwdParams kp;
-  int st = build_bwd(a, &kp, allow_fused);
-  if (st || (int64_t)a->p.batch * a->p.seq_len == 0) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if ((st = dispatch<Dq>(a->p, kp, s))) return st;
-  return dispatch<Dkdv>(a->p, kp, s);
 }
 
 }  // namespace
@@ -242,7 +211,8 @@ int swa_selftest_wait_timeout(int limit_us, void* stream) {
 
 size_t swa_bwd_workspace_size(const SwaProblem* p) {
   if (!p) return 0;
-  return workspace_bytes(*p, true);
+  if (check_problem(*p) != SWA_OK) return delta_bytes(*p);
+  return delta_bytes(*p) + partial_bytes(*p);
 }
 
 int swa_fwd(const SwaFwdArgs* a, void* stream) {
@@ -286,7 +256,15 @@ int swa_bwd_dkdv(const SwaBwdArgs* a, void* stream) {
   return dispatch<Dkdv>(a->p, kp, static_cast<cudaStream_t>(stream));
 }
 
-int swa_bwd(const SwaBwdArgs* a, void* stream) { return run_bwd(a, stream, true); }
+int swa_bwd(const SwaBwdArgs* a, void* stream) {
+  swa::BwdParams kp;
+  int st = build_bwd(a, &kp);
+  if (st || (int64_t)a->p.batch * a->p.seq_len == 0) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the dQ pass also computes Delta = rowsum(dO * O) into the workspace for the dK/dV pass
+  if ((st = dispatch<Dq>(a->p, kp, s))) return st;
+  return dispatch<Dkdv>(a->p, kp, s);
+}
 
 }  // extern "C"
 
@@ -326,13 +304,11 @@ extern "C" int swa_bwd_no_alloc(const SwaBwdArgs* a, void* stream) {
   if (!a) return SWA_ERR_INVALID_ARG;
   int st = check_problem(a->p);
   if (st) return st;
-  // the fused sink partials grow with L; without them the scratch covers more problems
-  const bool fused = workspace_bytes(a->p, true) <= SWA_NO_ALLOC_SCRATCH_BYTES;
-  if (!fused && workspace_bytes(a->p, false) > SWA_NO_ALLOC_SCRATCH_BYTES) return SWA_ERR_TOO_LARGE;
+  if (swa_bwd_workspace_size(&a->p) > SWA_NO_ALLOC_SCRATCH_BYTES) return SWA_ERR_TOO_LARGE;
   void* scratch = nullptr;
   if ((st = no_alloc_scratch(&scratch))) return st;
   SwaBwdArgs b = *a;
   b.workspace = scratch;
   b.workspace_bytes = SWA_NO_ALLOC_SCRATCH_BYTES;
-  return run_bwd(&b, stream, fused);
+  return swa_bwd(&b, stream);
 }

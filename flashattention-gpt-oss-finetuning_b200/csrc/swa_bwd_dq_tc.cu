@@ -8,19 +8,7 @@
 //   P  = 2^(S * scale*log2e - LSE_row), masked;  dS = P (dP - Delta_row) -> TMEM, 16-bit
 //        (warps 4..19: each thread owns one query row and 16 key columns)
 //   dQ += dS K                     (A = dS from TMEM, B = K MN-major smem) -> TMEM
-// and dQ * scale is written once per item.
-//
-// Far sink pairs (instantiation FUSED: SinkSplit with nf > 0, D >= 64): for a query tile at
-// or past the far tile qf0 the first segment is the sink segment (sb <= 32 keys from key 0).
-// Its elementwise pass also stages [dS | P] of the sink keys (rows >= rfar, zero elsewhere)
-// as one MN-major [128 rows x 64] B operand over the item's O tile (dead once Delta is
-// formed), and warp 3 issues, per 16-row K step, [Q^T; dO^T] [dS | P] (M = 2D, N = 64) into
-// the idle dQ buffer of the other parity (for D = 128, Q^T and dO^T as two M = 128 MMAs).
-// Its diagonal blocks are dK_sink^T = Q^T dS and dV_sink^T = dO^T P; the epilogue writes
-// them as fp32 partials (one slot per query head and far tile, added by the sink-row
-// reduction after the dK/dV pass) before it hands that dQ buffer back.
-//
-// S and dP have NB = 3 TMEM buffers (2 for
+// and dQ * scale is written once per item.  S and dP have NB = 3 TMEM buffers (2 for
 // D = 128) and dS is written back over the S columns each warp has read; S / dP of segment t
 // are issued as soon as the dQ MMAs of segment t - NB have completed, so S runs ahead of the
 // elementwise warps.
@@ -31,8 +19,7 @@
 // [B, Hq, round_up(L, 64)] buffers (+inf / 0 past L), so padded query rows contribute zero.
 //
 // Warp roles (24 warps, 768 threads): warp 0 TMA producer, warp 1 issues the S / dP MMAs and
-// warp 2 the dQ MMAs (one thread each; a buffer-release barrier orders them), warp 3 the far
-// sink MMAs (FUSED),
+// warp 2 the dQ MMAs (one thread each; a buffer-release barrier orders them),
 // warps 4..19 elementwise: four warps per TMEM lane quadrant, 16 key columns each, so that
 // every scheduler has four independent elementwise warps to hide the TMEM and special-
 // function latencies; warps 20..23 epilogue: dQ is double-buffered in TMEM, so writing back
@@ -72,9 +59,6 @@ struct DqCfg {
   static constexpr int KV_BYTES = BN * D * 2;        // one K or V segment
   static constexpr int NST = D <= 64 ? 6 : 3;        // K/V stages
   static constexpr int SMEM = 1024 + NQB * ITEM + NST * 2 * KV_BYTES;
-  // FUSED: [dS | P] of the sink keys, [128 rows x 64] with 128-byte rows, over the O tile
-  static constexpr int CAP_ROWB = 128, CAP_BYTES = 128 * CAP_ROWB;
-  static_assert(D < 64 || CAP_BYTES <= QT_BYTES, "sink staging must fit the O tile");
   // dS of a segment overwrites its S columns: key columns [16k, 16k+16) of S hold, after the
   // elementwise pass, dS keys 16k..16k+15 in [16k, 16k+8) (the A operand of MMA K-step k).
   static constexpr int S_COL = 0, DP_COL = 64 * NB, DQ_COL = 128 * NB;  // dQ: 2 buffers of D
@@ -85,10 +69,9 @@ struct DqCfg {
   static constexpr int THREADS = 128 + 128 * NGRP + 128;
 };
 
-template <typename T, int D, bool FUSED>
+template <typename T, int D>
 __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(const __grid_constant__ DqTmaps tm,
                                                            const BwdParams p, int* err) {
-  static_assert(!FUSED || D >= 64, "the far sink MMAs need M = D >= 64");
   using C = DqCfg<D>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ unsigned char smem_raw[];
@@ -100,8 +83,6 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
   __shared__ uint64_t bar_q_full[C::NQB], bar_q_empty[C::NQB], bar_dready[C::NQB];
   __shared__ uint64_t bar_full[C::NST], bar_empty[C::NST];
   __shared__ uint64_t bar_s[C::NB], bar_p[C::NB], bar_rel[C::NB], bar_acc[2], bar_acc_free[2];
-  // FUSED: sink staging done (two, by far-tile parity), the other dQ buffer read, sink MMAs done
-  __shared__ uint64_t bar_cap[2], bar_dqr, bar_sink;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
 
@@ -117,7 +98,7 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
     for (int s = 0; s < C::NQB; ++s) {
       mbar_init(&bar_q_full[s], 1);
       mbar_init(&bar_dready[s], 128);
-      mbar_init(&bar_q_empty[s], FUSED ? 2 : 1);  // FUSED: the sink MMA thread also releases
+      mbar_init(&bar_q_empty[s], 1);
     }
     for (int s = 0; s < C::NST; ++s) {
       mbar_init(&bar_full[s], 1);
@@ -131,10 +112,7 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bar_acc[s], 1);
       mbar_init(&bar_acc_free[s], 128);
-      mbar_init(&bar_cap[s], 256);  // the elementwise warps of the first two column groups
     }
-    mbar_init(&bar_dqr, 128);
-    mbar_init(&bar_sink, 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -291,53 +269,6 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
         record_error(err, 1);
       }
     }
-  } else if (warp == 3) {
-    // ------------------------------------------------------------------ MMA issuer: far sink
-    if constexpr (FUSED) {
-      if (lane == 0 && !dead) {
-        // [Q^T; dO^T] (M = 2D <= 128: Q and dO tiles are adjacent MN-major chunks) or, for
-        // D = 128, Q^T and dO^T separately; B = staged [dS | P], MN-major, 128-byte rows
-        constexpr int MA = D == 64 ? 128 : D;
-        constexpr uint32_t id_k = idesc_f16(MA, 64, kBf16, true, true);
-        const uint64_t itmn0 = sdesc(saddr(ITs), C::BM * C::ROWB, 8 * C::ROWB, C::SWZ);
-        const uint64_t cap0 = sdesc(saddr(ITs + C::O_OFF), C::CAP_BYTES, 8 * C::CAP_ROWB, kSw128);
-        int qi = 0, kf = 0;
-        bool ok = true;
-        for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-          int b, h, qt;
-          decode_item(it, Hq, n_qt, &b, &h, &qt);
-          if (fwd_schedule(qt * C::BM, L, W, S, p.sink_box).n() == 0) continue;
-          const int qb = qi % C::NQB;
-          if (qt >= p.qf0) {
-            if (!(ok = mbar_wait(&bar_cap[kf & 1], (kf >> 1) & 1, &abort_sh))) break;
-            // the other dQ buffer: the epilogue has read the previous item's dQ from it
-            if (!(ok = mbar_wait(&bar_dqr, kf & 1, &abort_sh))) break;
-            tc_fence_after();
-            const uint64_t aq = sdesc_add(itmn0, qb * C::ITEM);
-            const uint64_t bc = sdesc_add(cap0, qb * C::ITEM);
-            const uint32_t acc = tmem + C::DQ_COL + ((qi + 1) & 1) * D;
-#pragma unroll
-            for (int ks = 0; ks < C::BM / 16; ++ks) {
-              const uint64_t a = sdesc_add(aq, ks * 16 * C::ROWB), bm = sdesc_add(bc, ks * 16 * C::CAP_ROWB);
-              if constexpr (D == 64) {
-                mma_ss(acc, a, bm, id_k, ks > 0 ? 1u : 0u);
-              } else {
-                mma_ss(acc, a, bm, id_k, ks > 0 ? 1u : 0u);                                    // Q^T
-                mma_ss(acc + 64, sdesc_add(a, C::QT_BYTES), bm, id_k, ks > 0 ? 1u : 0u);     // dO^T
-              }
-            }
-            mma_commit(&bar_sink);
-            ++kf;
-          }
-          mma_commit(&bar_q_empty[qb]);  // Q / dO / staging no longer read by this thread
-          ++qi;
-        }
-        if (!ok) {
-          abort_sh = 1;
-          record_error(err, 1);
-        }
-      }
-    }
   } else if (warp >= C::EPI_WARP) {
     // ------------------------------------------------------------------ epilogue (4 warps)
     // Per item: Delta = rowsum(dO * O) of the NEXT item (from its staged dO and O tiles; into
@@ -347,15 +278,14 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
     const int r = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     constexpr uint32_t SWM = C::ROWB / 16 - 1;  // swizzle: 16-byte unit ^= (offset >> 7) & SWM
-    int qi = 0, dqi = 0, it_d = blockIdx.x, qt_d = -1;
+    int qi = 0, dqi = 0, it_d = blockIdx.x;
     bool ok = !dead;
-    // Delta of the next item with segments (its tile in qt_d); false when there is none
+    // Delta of the next item with segments; false when there is none
     auto delta_next = [&]() -> bool {
       for (; it_d < n_items; it_d += gridDim.x) {
         int b, h, qt;
         decode_item(it_d, Hq, n_qt, &b, &h, &qt);
         if (fwd_schedule(qt * C::BM, L, W, S, p.sink_box).n() == 0) continue;
-        qt_d = qt;
         const int qb = dqi % C::NQB;
         if (ok) ok = mbar_wait(&bar_q_full[qb], (dqi / C::NQB) & 1, &abort_sh);
         float acc = 0.f;
@@ -387,60 +317,14 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
       return false;
     };
     delta_next();
-    // FUSED: a far tile's sink MMAs borrow the dQ buffer of the previous item, so that item's
-    // acc_free is held back (free_held) until the sink partials have been read out.
-    int kf = 0;
-    bool free_held = false;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
       int b, h, qt;
       decode_item(it, Hq, n_qt, &b, &h, &qt);
       const int i = qt * C::BM + r;
       const int n = fwd_schedule(qt * C::BM, L, W, S, p.sink_box).n();
       const bool have = n > 0;
-      const bool far = FUSED && have && qt >= p.qf0;
-      if (far) {  // the previous item's dQ has been read (or there was none)
-        tc_fence_before();
-        mbar_arrive(&bar_dqr);
-      }
-      bool next_far = false;
       if (have) {
-        next_far = delta_next() && FUSED && qt_d >= p.qf0;  // the following item's Delta
-        if constexpr (FUSED) {
-          if (far) {
-            // dK_sink^T = Q^T dS in lanes [0, D) columns [0, 32) of the borrowed buffer, dV_sink^T
-            // = dO^T P in lanes [64, 128) columns [32, 64) (D = 64) or lanes [0, 128) columns
-            // [96, 128) (D = 128); row m of an M = 128 accumulator is TMEM lane m
-            if (ok) ok = mbar_wait(&bar_sink, kf & 1, &abort_sh);
-            tc_fence_after();
-            if (ok) {
-              const uint32_t tb = tmem + C::DQ_COL + ((qi + 1) & 1) * D + lane_off;
-              const int slot = (h % G) * p.nf + (qt - p.qf0);
-              float* base = p.partf + ((int64_t)(b * p.Hkv + h / G) * G * p.nf + slot) * 2 * S * D;
-#pragma unroll 1
-              for (int part = 0; part < (D == 64 ? 1 : 2); ++part) {
-                const int kv = D == 64 ? (quad >> 1) : part;  // 0: dK, 1: dV
-                const int d = D == 64 ? r & 63 : r;
-                const uint32_t c0 = D == 64 ? 32 * kv : 96 * kv;
-                float* dst = base + (int64_t)kv * S * D + d;
-#pragma unroll 1
-                for (int j0 = 0; j0 < S; j0 += 16) {
-                  uint32_t v[16];
-                  tmem_ld16(tb + c0 + j0, v);
-                  tmem_ld_wait();
-#pragma unroll
-                  for (int j = 0; j < 16; ++j)
-                    if (j0 + j < S) dst[(int64_t)(j0 + j) * D] = __uint_as_float(v[j]);
-                }
-              }
-            }
-            if (free_held) {  // the previous item's dQ buffer goes back to the dQ MMA thread
-              tc_fence_before();
-              mbar_arrive(&bar_acc_free[(qi + 1) & 1]);
-              free_held = false;
-            }
-            ++kf;
-          }
-        }
+        delta_next();  // the following item's Delta overlaps this item's last segments
         if (ok) ok = mbar_wait(&bar_acc[qi & 1], (qi >> 1) & 1, &abort_sh);
         tc_fence_after();
       } else if (i < p.lse_ld) {
@@ -470,10 +354,7 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
       }
       if (have) {
         tc_fence_before();
-        if (next_far)
-          free_held = true;  // released after the next tile's sink read-out
-        else
-          mbar_arrive(&bar_acc_free[qi & 1]);
+        mbar_arrive(&bar_acc_free[qi & 1]);
         ++qi;
       }
     }
@@ -488,7 +369,7 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
     const int r = quad * 32 + lane;  // query row of the tile (TMEM lane)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float sl2 = p.scale_log2;
-    int qi = 0, gs = 0, kf = 0;
+    int qi = 0, gs = 0;
     bool ok = !dead;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
       int b, h, qt;
@@ -505,42 +386,23 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
         lse_r = st_rows[r];
         dl_r = st_rows[128 + r];
       }
-      // One segment; CAP (FUSED, the sink segment of a far tile): the first two column groups
-      // also stage [dS | P] of the sink keys, rows >= rfar (zero elsewhere), for the sink MMAs.
-      // Kept out of the loop below so that ordinary segments carry none of its registers.
-      auto segment = [&](int t, auto cap_tag) -> bool {
-        constexpr bool CAP = decltype(cap_tag)::value;
+      for (int t = 0; t < n && ok; ++t) {
         const int gt = gs + t;
         const int bb = gt % C::NB;
-        if (!mbar_wait(&bar_s[bb], (gt / C::NB) & 1, &abort_sh)) return false;
+        if (!(ok = mbar_wait(&bar_s[bb], (gt / C::NB) & 1, &abort_sh))) break;
         tc_fence_after();
         int key0, rows;
         sc.seg(t, &key0, &rows);
-        unsigned char* cap_base = ITs + (qi % C::NQB) * C::ITEM + C::O_OFF;
-        // 16-byte unit u of staging row r sits at r * 128 + ((u ^ (r % 8)) * 16)
-        auto cap_store = [&](int unit, const uint32_t* w) {
-#pragma unroll
-          for (int hv = 0; hv < 2; ++hv) {
-            uint32_t off = r * C::CAP_ROWB + (unit + hv) * 16;
-            off ^= ((off >> 7) & 7u) << 4;
-            *reinterpret_cast<uint4*>(cap_base + off) = make_uint4(w[4 * hv], w[4 * hv + 1], w[4 * hv + 2], w[4 * hv + 3]);
-          }
-        };
 #pragma unroll
         for (int ch = 0; ch < CPG / 16; ++ch) {
           const int col = grp * CPG + ch * 16;  // first of this chunk's 16 key columns
           const int kc0 = key0 + col;
           const uint32_t tdS = tmem + C::S_COL + bb * 64 + col + lane_off;  // over this chunk's S
-          const bool cap = CAP && col < 32;
-          const uint32_t z[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
           if (col < rows) {
             const int kc1 = min(kc0 + 16, key0 + rows);
             if (block_none_visible(rw0, rw0 + 32, kc0, kc1, W, S, L)) {
+              const uint32_t z[8] = {0u};
               tmem_st8(tdS, z);
-              if (cap) {
-                cap_store(col / 8, z);
-                cap_store(4 + col / 8, z);
-              }
             } else {
               const bool full = kc1 == kc0 + 16 && block_all_visible(rw0, rw0 + 32, kc0, kc1, W, S, L);
               float s[16], dp[16];
@@ -552,10 +414,10 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
               const int c_hi = i - kc0;
               const int c_lo = i - W + 1 - kc0;
               const int c_sk = S - kc0;
-              uint32_t dw[8], pw[8];
+              uint32_t dw[8];
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
-                float d2[2], p2[2];
+                float d2[2];
 #pragma unroll
                 for (int h2 = 0; h2 < 2; ++h2) {
                   const int c = 2 * e + h2;
@@ -563,42 +425,17 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
                   const float ds = pr * (dp[c] - dl_r);
                   const bool vis = full || (c < c_end && c <= c_hi && (c >= c_lo || c < c_sk));
                   d2[h2] = vis ? ds : 0.f;
-                  if constexpr (CAP) p2[h2] = vis ? pr : 0.f;
                 }
                 dw[e] = Pack<T>::pack(d2[0], d2[1]);
-                if constexpr (CAP) pw[e] = Pack<T>::pack(p2[0], p2[1]);
               }
               tmem_st8(tdS, dw);
-              if (cap) {
-                const bool row_far = i >= p.rfar;
-                cap_store(col / 8, row_far ? dw : z);
-                cap_store(4 + col / 8, row_far ? pw : z);
-              }
             }
-          } else if (cap) {
-            cap_store(col / 8, z);
-            cap_store(4 + col / 8, z);
           }
-        }
-        if (CAP && grp * CPG < 32) {
-          fence_proxy_async_smem();  // generic-proxy writes before the sink MMAs read them
-          mbar_arrive(&bar_cap[kf & 1]);
         }
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&bar_p[bb]);
-        return true;
-      };
-      int t = 0;
-      if constexpr (FUSED) {
-        if (qt >= p.qf0 && n > 0) {
-          if (ok) ok = segment(0, std::true_type{});
-          if (!ok && grp * CPG < 32) mbar_arrive(&bar_cap[kf & 1]);  // keep the count on failure
-          ++kf;
-          t = 1;
-        }
       }
-      for (; t < n && ok; ++t) ok = segment(t, std::false_type{});
       if (n > 0 && ok) {
         gs += n;
         ++qi;
@@ -632,11 +469,7 @@ cudaError_t launch_bwd_dq_tc(const BwdParams& p0, cudaStream_t st, int* err) {
             make_tmap_bhld(&tm.o, p.o, p.B, p.Hq, p.L, D, p.so.b, p.so.h, p.so.l, C::CW, C::BM) &&
             make_tmap_rows_f32(&tm.lse, p.lse, (long long)p.B * p.Hq, p.lse_ld, p.lse_ld, 64);
   if (!ok) return cudaErrorInvalidValue;
-  // far sink pairs ride along only with D >= 64 (M of the sink MMAs) and NGRP = 4 (the
-  // first two column groups cover the 32 staged keys)
-  constexpr bool kCanFuse = D >= 64 && C::NGRP == 4;
-  if (p.nf > 0 && !kCanFuse) return cudaErrorInvalidConfiguration;
-  auto kern = (kCanFuse && p.nf > 0) ? bwd_dq_tc_kernel<T, D, kCanFuse> : bwd_dq_tc_kernel<T, D, false>;
+  auto kern = bwd_dq_tc_kernel<T, D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);

@@ -102,12 +102,6 @@ __device__ __forceinline__ void query_range(int k0, int BN, int BM, int L, int W
 // Every such CTA writes fp32 partial sums of the sink rows to the workspace, and a reduction
 // adds them in a fixed order (deterministic).
 // ---------------------------------------------------------------------------------------
-//
-// Fused variant (S <= kFusedSinkMax, D >= 64): the far pairs are not given to dK/dV items at
-// all.  The dQ pass already computes P and dS of the sink keys for every query tile (its
-// first key segment); for the far query tiles it also forms dV_sink^T = dO^T P_sink and
-// dK_sink^T = Q^T dS_sink on the tensor cores and writes them as fp32 partials, one slot per
-// (query head, far 128-row query tile).  Rows below `rfar` stay with the near dK/dV item.
 struct SinkSplit {
   int nst;  // key tiles that hold sinks
   int sp;   // rows kept per sink tile in the partials (multiple of 16, <= key tile)
@@ -115,12 +109,7 @@ struct SinkSplit {
   int ch;   // far (query head, query tile) steps per chunk
   int bn;   // key tile
   int bm;   // query tile
-  int nf;   // fused: far 128-row query tiles per query head (0: not fused)
-  int qf0;  // fused: first far 128-row query tile
-  int rfar; // fused: first far query row (near rows below it stay with the dK/dV item)
 };
-
-constexpr int kFusedSinkMax = 32;  // sink keys the dQ pass can carry (one segment, N <= 32)
 
 constexpr int kSplitChunkSteps = 64;  // steps per far chunk
 constexpr int kDkdvKeyTile = 128;     // key tile of the dK/dV pass
@@ -154,14 +143,10 @@ __host__ __device__ inline int far_steps(int kt, int L, int W, int G, int bn, in
   return start < n_qt ? G * (n_qt - start) : 0;
 }
 
-__host__ __device__ inline SinkSplit sink_split(int L, int W, int S, int G, int bn, int bm, int D = 0,
-                                                bool allow_fused = false) {
+__host__ __device__ inline SinkSplit sink_split(int L, int W, int S, int G, int bn, int bm) {
   SinkSplit ss;
   ss.bn = bn;
   ss.bm = bm;
-  ss.nf = 0;
-  ss.qf0 = 0;
-  ss.rfar = 0;
   const int sk = S < L ? S : L;
   ss.nst = sk > 0 ? (sk + bn - 1) / bn : 0;
   const int s16 = (S + 15) / 16 * 16;
@@ -172,25 +157,12 @@ __host__ __device__ inline SinkSplit sink_split(int L, int W, int S, int G, int 
     const int c = (far_steps(kt, L, W, G, bn, bm) + ss.ch - 1) / ss.ch;
     if (c > ss.nc) ss.nc = c;
   }
-  if (allow_fused && ss.nst == 1 && S <= kFusedSinkMax && D >= 64 && ss.nc > 0) {
-    const int n_qt128 = (L + 127) / 128;
-    ss.rfar = far_qt_lo(0, L, W, bn, bm) * bm;
-    ss.qf0 = ss.rfar / 128;
-    ss.nf = n_qt128 - ss.qf0;
-    ss.nc = 0;
-  }
   return ss;
 }
 
-// Floats of the near / far-chunk partials: (1 + nc) slots x B x Hkv x nst tiles x {dK, dV} x
-// sp rows x D.
+// Floats of sink partials: (1 + nc) slots x B x Hkv x nst tiles x {dK, dV} x sp rows x D.
 __host__ __device__ inline long long sink_partial_floats(const SinkSplit& ss, int B, int Hkv, int D) {
   return (long long)(1 + ss.nc) * B * Hkv * ss.nst * 2 * ss.sp * D;
-}
-
-// Floats of the fused far partials: B x Hkv x (G x nf) slots x {dK, dV} x S rows x D.
-__host__ __device__ inline long long sink_fused_floats(const SinkSplit& ss, int B, int Hkv, int G, int S, int D) {
-  return (long long)B * Hkv * G * ss.nf * 2 * S * D;
 }
 
 // ---------------------------------------------------------------------------------------

@@ -41,8 +41,6 @@ struct BwdParams {
   float* part;       // sink-row partial sums of dK / dV (workspace, after delta)
   int nst, sp, nc, ch;  // SinkSplit
   int bn_split, bm_split;  // key / query tile sizes the split was made for
-  float* partf;      // fused far partials [B][Hkv][G * nf][{dK, dV}][S][D] (dQ pass)
-  int nf, qf0, rfar;  // SinkSplit, fused variant (nf = 0: not fused)
 };
 
 }  // namespace swa

@@ -93,18 +93,6 @@ def test_window_sink_grid(d, w, s):
     check(q, k, v, do, w, s)
 
 
-@pytest.mark.parametrize("d", [64, 128])
-@pytest.mark.parametrize("w,s", [(160, 4), (100, 1), (64, 16), (200, 17), (96, 32), (96, 33),
-                                 (0, 20), (1, 8)])
-def test_far_sink_pairs(d, w, s):
-    # S <= 32 with D >= 64: the dQ pass carries the sink pairs of rows past the dK/dV item's
-    # query range (W = 160 puts that boundary inside a 128-row tile); S = 33 takes the
-    # far-chunk items of the dK/dV pass instead
-    dtype = torch.bfloat16 if (w + s) % 2 else torch.float16
-    q, k, v, do = rand((2, 4, 1000, d), (2, 2, 1000, d), dtype, 7000 + d + w + s)
-    check(q, k, v, do, w, s)
-
-
 def test_no_visible_keys_gives_zero():
     q, k, v, do = rand((1, 2, 70, 32), (1, 2, 70, 32), torch.bfloat16, 9)
     o, dq, dk, dv = run_ours(q, k, v, do, 0, 0)
