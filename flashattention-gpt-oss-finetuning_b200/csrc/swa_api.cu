@@ -81,7 +81,15 @@ int effective_window(int w, int L) { return w < 0 ? 0 : (w > L ? (L > 0 ? L : 1)
 
 template <template <typename, int> class F, typename P>
 int dispatch(const SwaProblem& pr, const P& kp, cudaStream_t st) {
-  cudaError_t e = cudaErrorInvalidValue;
+  // The TMA descriptors are encoded through the driver API, which needs a current context in
+  // the calling thread.  A host thread that has only ever been told its device by a framework
+  // (an autograd worker, say) may have none yet: making the device current again binds the
+  // primary context.
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return record(e);
+  e = cudaErrorInvalidValue;
 #define SWA_D(T)                                          \
   switch (pr.head_dim) {                                  \
     case 16: e = F<T, 16>::run(kp, st); break;            \

@@ -93,6 +93,17 @@ def test_window_sink_grid(d, w, s):
     check(q, k, v, do, w, s)
 
 
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("w,s", [(160, 4), (100, 1), (64, 16), (200, 17), (96, 32), (96, 33),
+                                 (0, 20), (1, 8)])
+def test_far_sink_pairs(d, w, s):
+    # sink keys seen by rows far past their window: the far-chunk items of the dK/dV pass
+    # and the sink-row reduction (W = 160 puts the near/far boundary inside a 128-row tile)
+    dtype = torch.bfloat16 if (w + s) % 2 else torch.float16
+    q, k, v, do = rand((2, 4, 1000, d), (2, 2, 1000, d), dtype, 7000 + d + w + s)
+    check(q, k, v, do, w, s)
+
+
 def test_no_visible_keys_gives_zero():
     q, k, v, do = rand((1, 2, 70, 32), (1, 2, 70, 32), torch.bfloat16, 9)
     o, dq, dk, dv = run_ours(q, k, v, do, 0, 0)
@@ -175,3 +186,47 @@ def test_baseline_configs_reduced(name, kw):
     w = wl.CONFIGS[name].replace(**kw)
     q, k, v, do = wl.make_inputs(w)
     check(q, k, v, do, w.window_size, w.sink_size, chunked=True)
+
+
+def test_pinned_host_step_through_autograd():
+    # a training step as a user runs it: pinned host inputs copied without blocking, forward
+    # and backward through the autograd Function (the backward runs on autograd's own thread)
+    q, k, v, do = (t.pin_memory() for t in rand((1, 8, 700, 64), (1, 2, 700, 64), torch.bfloat16, 77))
+    dev = torch.device("cuda:0")
+    qd, kd, vd, dod = (t.to(dev, non_blocking=True) for t in (q, k, v, do))
+    for t in (qd, kd, vd):
+        t.requires_grad_()
+    o = pkg().flash_swda_with_sink(qd, kd, vd, 64, 4)
+    o.backward(dod)
+    assert_device_ok(dev)
+    ref = orc.backward(q.float(), k.float(), v.float(), do.float(), 64, 4)
+    for a, r in zip((o, qd.grad, kd.grad, vd.grad), ref):
+        assert _rel(a, r) <= TOL[torch.bfloat16]
+
+
+def test_backward_from_a_fresh_host_thread():
+    # a thread that has made no CUDA runtime call of its own (as autograd's worker is when it
+    # runs the first backward) has no current context; the library must bind one before it
+    # encodes its TMA descriptors
+    import threading
+    f = submodule("flash_attention_gpt_oss")
+    q, k, v, do = rand((1, 4, 300, 32), (1, 2, 300, 32), torch.float16, 78)
+    dev = torch.device("cuda:0")
+    qd, kd, vd, dod = (t.to(dev) for t in (q, k, v, do))
+    o, lse = f.swa_forward(qd, kd, vd, 50, 4)
+    out = {}
+
+    def work():
+        try:
+            out["grads"] = f.swa_backward(qd, kd, vd, o, lse, dod, 50, 4)
+            torch.cuda.synchronize(dev)
+        except Exception as e:  # reported below, in the test's own thread
+            out["error"] = e
+
+    th = threading.Thread(target=work)
+    th.start()
+    th.join()
+    assert "error" not in out, out.get("error")
+    ref = orc.backward(q.float(), k.float(), v.float(), do.float(), 50, 4)
+    for a, r in zip(out["grads"], ref[1:]):
+        assert _rel(a, r) <= TOL[torch.float16]
