@@ -322,8 +322,8 @@ def run_ours(args, w_job, rank, world, local_rank):
 
 
 # DRAM bytes (read + write) per launch from one ncu capture, keyed by (workload, kernel)
-# (profiles/dkdv_tc_cfg2_ncu.md: 576.5 MB read + 27.1 MB written).
-TRAFFIC: dict = {("cfg2_gptoss_swa", "bwd_dkdv"): 603_651_584}
+# (the dK/dV capture of the cfg2 step: 581.4 MB read + 28.8 MB written).
+TRAFFIC: dict = {("cfg2_gptoss_swa", "bwd_dkdv"): 610_271_744}
 
 
 def main():
