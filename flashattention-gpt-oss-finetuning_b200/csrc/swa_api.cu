@@ -133,7 +133,8 @@ size_t delta_bytes(const SwaProblem& p) {
 
 swa::SinkSplit split_of(const SwaProblem& p) {
   return swa::sink_split(p.seq_len, effective_window(p.window_size, p.seq_len), p.sink_size,
-                         p.n_q_heads / p.n_kv_heads, swa::kDkdvKeyTile, swa::kDkdvQueryTile);
+                         p.n_q_heads / p.n_kv_heads, swa::kDkdvKeyTile, swa::kDkdvQueryTile, p.batch,
+                         p.n_kv_heads, p.head_dim);
 }
 
 size_t partial_bytes(const SwaProblem& p) {
@@ -170,6 +171,7 @@ int build_bwd(const SwaBwdArgs* a, swa::BwdParams* kp) {
   kp->part = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + delta_bytes(p));
   kp->nst = ss.nst; kp->sp = ss.sp; kp->nc = ss.nc; kp->ch = ss.ch;
   kp->bn_split = ss.bn; kp->bm_split = ss.bm;
+  kp->fk_c = ss.fk_c; kp->fk_u = ss.fk_u; kp->rfar = ss.rfar; kp->qf0 = ss.qf0; kp->nf = ss.nf;
   return SWA_OK;
 }
 

@@ -445,43 +445,64 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
   if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
-// Sink rows: dK = scale * sum of partials, dV = sum, added in slot order (deterministic).
+// Sink rows: dK = scale * sum of partials, dV = sum, added in a fixed slot order
+// (deterministic).  One CTA per (batch, KV head, sink tile) and 32 consecutive outputs of its
+// {dK, dV} x sp x D block: each of the 8 warps sums a contiguous range of slots, and warp 0
+// adds the 8 range sums in order.
 template <typename T, int D>
 __global__ void __launch_bounds__(256) bwd_sink_reduce_kernel(BwdParams p) {
-  const int64_t n = (int64_t)p.B * p.Hkv * p.nst * p.sp * D;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= n) return;
-  const int d = (int)(idx % D);
-  int64_t rest = idx / D;
-  const int r = (int)(rest % p.sp);
-  rest /= p.sp;
-  const int kt = (int)(rest % p.nst);
+  __shared__ float part_sum[8][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_out = 2 * p.sp * D;
+  const int n_oc = (n_out + 31) / 32;
+  int rest = blockIdx.x;
+  const int oc = rest % n_oc;
+  rest /= n_oc;
+  const int kt = rest % p.nst;
   rest /= p.nst;
-  const int kvh = (int)(rest % p.Hkv);
-  const int b = (int)(rest / p.Hkv);
+  const int kvh = rest % p.Hkv;
+  const int b = rest / p.Hkv;
+  const int o = oc * 32 + lane;
+  const int part = o / (p.sp * D);
+  const int r = (o / D) % p.sp;
+  const int d = o % D;
   const int j = kt * p.bn_split + r;
-  if (j >= p.S || j >= p.L) return;
-  const int G = p.Hq / p.Hkv;
-  const int slots = 1 + (far_steps(kt, p.L, p.W, G, p.bn_split, p.bm_split) + p.ch - 1) / p.ch;
-  float sk = 0.f, sv = 0.f;
-  for (int s = 0; s < slots; ++s) {
-    const float* pk = p.part + ((((int64_t)s * p.B + b) * p.Hkv + kvh) * p.nst + kt) * 2 * p.sp * D;
-    sk += pk[(int64_t)r * D + d];
-    sv += pk[(int64_t)(p.sp + r) * D + d];
+  const bool valid = o < n_out && j < p.S && j < p.L;
+  SinkSplit ss;
+  ss.bn = p.bn_split; ss.bm = p.bm_split; ss.ch = p.ch; ss.fk_c = p.fk_c; ss.fk_u = p.fk_u;
+  const int n_slots = sink_slots(ss, kt, p.L, p.W, p.Hq / p.Hkv);
+  const int s_lo = n_slots * warp / 8, s_hi = n_slots * (warp + 1) / 8;
+  float acc = 0.f;
+  if (valid) {
+    const int64_t stride = (int64_t)p.B * p.Hkv * p.nst * 2 * p.sp * D;
+    const float* src = p.part + (((int64_t)b * p.Hkv + kvh) * p.nst + kt) * 2 * p.sp * D + o;
+#pragma unroll 4
+    for (int sl = s_lo; sl < s_hi; ++sl) acc += src[sl * stride];
   }
-  T* dk = static_cast<T*>(p.dk) + b * p.sdk.b + kvh * p.sdk.h + (int64_t)j * p.sdk.l + d;
-  T* dv = static_cast<T*>(p.dv) + b * p.sdv.b + kvh * p.sdv.h + (int64_t)j * p.sdv.l + d;
-  *dk = Pack<T>::from(sk * p.scale);
-  *dv = Pack<T>::from(sv);
+  part_sum[warp][lane] = acc;
+  __syncthreads();
+  if (warp != 0 || !valid) return;
+  float v = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) v += part_sum[w][lane];
+  if (part == 0) {
+    T* dk = static_cast<T*>(p.dk) + b * p.sdk.b + kvh * p.sdk.h + (int64_t)j * p.sdk.l + d;
+    *dk = Pack<T>::from(v * p.scale);
+  } else {
+    T* dv = static_cast<T*>(p.dv) + b * p.sdv.b + kvh * p.sdv.h + (int64_t)j * p.sdv.l + d;
+    *dv = Pack<T>::from(v);
+  }
 }
 
 template <typename T, int D>
 cudaError_t launch_sink_reduce(const BwdParams& p, cudaStream_t st) {
-  const int64_t n = (int64_t)p.B * p.Hkv * p.nst * p.sp * D;
+  const long long n = (long long)p.B * p.Hkv * p.nst * ((2 * p.sp * D + 31) / 32);
   if (n == 0) return cudaSuccess;
-  bwd_sink_reduce_kernel<T, D><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p);
+  bwd_sink_reduce_kernel<T, D><<<(unsigned)n, 256, 0, st>>>(p);
   return cudaGetLastError();
 }
+
+template <typename T, int D> cudaError_t launch_sink_far(const BwdParams& p, cudaStream_t st, int* err);
 
 template <typename T, int D>
 cudaError_t launch_bwd_dkdv_tc(const BwdParams& p, cudaStream_t st, int* err) {
@@ -506,6 +527,7 @@ cudaError_t launch_bwd_dkdv_tc(const BwdParams& p, cudaStream_t st, int* err) {
   kern<<<grid, C::THREADS, C::SMEM, st>>>(tm, p, err);
   e = cudaGetLastError();
   if (e != cudaSuccess || p.nst == 0) return e;
+  if (p.fk_c > 0 && (e = launch_sink_far<T, D>(p, st, err)) != cudaSuccess) return e;
   return launch_sink_reduce<T, D>(p, st);
 }
 

@@ -102,14 +102,28 @@ __device__ __forceinline__ void query_range(int k0, int BN, int BM, int L, int W
 // Every such CTA writes fp32 partial sums of the sink rows to the workspace, and a reduction
 // adds them in a fixed order (deterministic).
 // ---------------------------------------------------------------------------------------
+//
+// Far-pair kernel (fk_c > 0: one sink tile, sp <= 32, D >= 64): the far pairs are not dK/dV
+// items at all.  bwd_sink_far_kernel takes, per far 128-row query tile (rows >= rfar), the
+// sink keys' S and dP on the tensor cores (N = sp), forms P and dS, and accumulates
+// [Q^T; dO^T] [dS | P] over a unit of fk_c consecutive (query head, far tile) items of one
+// (batch, KV head); unit u of a group writes partial slot 1 + u.  That kernel only streams Q
+// and dO once, where a far dK/dV step spends a whole 128-key tile step on 4 live rows.
 struct SinkSplit {
   int nst;  // key tiles that hold sinks
   int sp;   // rows kept per sink tile in the partials (multiple of 16, <= key tile)
-  int nc;   // far chunks per sink tile (the maximum over the sink tiles)
+  int nc;   // far chunks per sink tile (the maximum over the sink tiles); 0 with fk_c
   int ch;   // far (query head, query tile) steps per chunk
   int bn;   // key tile
   int bm;   // query tile
+  int fk_c;  // far-pair kernel: items per unit (0: far chunks in the dK/dV pass instead)
+  int fk_u;  // far-pair kernel: units per (batch, KV head)
+  int rfar;  // far-pair kernel: first far query row
+  int qf0;   // far-pair kernel: first 128-row query tile holding a far row
+  int nf;    // far-pair kernel: far 128-row query tiles per query head
 };
+
+constexpr int kFarUnitsTarget = 1024;  // far-pair units wanted in total (several per CTA)
 
 constexpr int kSplitChunkSteps = 64;  // steps per far chunk
 constexpr int kDkdvKeyTile = 128;     // key tile of the dK/dV pass
@@ -143,10 +157,12 @@ __host__ __device__ inline int far_steps(int kt, int L, int W, int G, int bn, in
   return start < n_qt ? G * (n_qt - start) : 0;
 }
 
-__host__ __device__ inline SinkSplit sink_split(int L, int W, int S, int G, int bn, int bm) {
+__host__ __device__ inline SinkSplit sink_split(int L, int W, int S, int G, int bn, int bm, int B = 0,
+                                                int Hkv = 0, int D = 0) {
   SinkSplit ss;
   ss.bn = bn;
   ss.bm = bm;
+  ss.fk_c = ss.fk_u = ss.rfar = ss.qf0 = ss.nf = 0;
   const int sk = S < L ? S : L;
   ss.nst = sk > 0 ? (sk + bn - 1) / bn : 0;
   const int s16 = (S + 15) / 16 * 16;
@@ -157,12 +173,28 @@ __host__ __device__ inline SinkSplit sink_split(int L, int W, int S, int G, int 
     const int c = (far_steps(kt, L, W, G, bn, bm) + ss.ch - 1) / ss.ch;
     if (c > ss.nc) ss.nc = c;
   }
+  if (ss.nst == 1 && ss.sp <= 32 && D >= 64 && ss.nc > 0 && B > 0 && Hkv > 0) {
+    ss.rfar = far_qt_lo(0, L, W, bn, bm) * bm;
+    ss.qf0 = ss.rfar / 128;
+    ss.nf = (L + 127) / 128 - ss.qf0;
+    const long long items = (long long)B * Hkv * G * ss.nf;
+    long long c = (items + kFarUnitsTarget - 1) / kFarUnitsTarget;
+    ss.fk_c = (int)(c < 2 ? 2 : c);
+    ss.fk_u = (G * ss.nf + ss.fk_c - 1) / ss.fk_c;
+    ss.nc = 0;
+  }
   return ss;
+}
+
+// Partial-sum slots of sink tile kt: the near item, then the far chunks or far-pair units.
+__host__ __device__ inline int sink_slots(const SinkSplit& ss, int kt, int L, int W, int G) {
+  if (ss.fk_c > 0) return 1 + ss.fk_u;
+  return 1 + (far_steps(kt, L, W, G, ss.bn, ss.bm) + ss.ch - 1) / ss.ch;
 }
 
 // Floats of sink partials: (1 + nc) slots x B x Hkv x nst tiles x {dK, dV} x sp rows x D.
 __host__ __device__ inline long long sink_partial_floats(const SinkSplit& ss, int B, int Hkv, int D) {
-  return (long long)(1 + ss.nc) * B * Hkv * ss.nst * 2 * ss.sp * D;
+  return (long long)(1 + (ss.fk_c > 0 ? ss.fk_u : ss.nc)) * B * Hkv * ss.nst * 2 * ss.sp * D;
 }
 
 // ---------------------------------------------------------------------------------------

@@ -41,6 +41,7 @@ struct BwdParams {
   float* part;       // sink-row partial sums of dK / dV (workspace, after delta)
   int nst, sp, nc, ch;  // SinkSplit
   int bn_split, bm_split;  // key / query tile sizes the split was made for
+  int fk_c, fk_u, rfar, qf0, nf;  // SinkSplit far-pair kernel fields (fk_c = 0: not used)
 };
 
 }  // namespace swa
