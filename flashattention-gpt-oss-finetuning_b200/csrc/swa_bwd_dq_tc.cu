@@ -414,19 +414,22 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
               const int c_hi = i - kc0;
               const int c_lo = i - W + 1 - kc0;
               const int c_sk = S - kc0;
+              // two columns per step on the packed fp32 pipe (same roundings as the scalar
+              // fma / sub / mul)
+              const float2 sl2v = make_float2(sl2, sl2), nlse = make_float2(-lse_r, -lse_r);
+              const float2 ndl = make_float2(-dl_r, -dl_r);
               uint32_t dw[8];
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
-                float d2[2];
-#pragma unroll
-                for (int h2 = 0; h2 < 2; ++h2) {
-                  const int c = 2 * e + h2;
-                  const float pr = fast_exp2(fmaf(s[c], sl2, -lse_r));
-                  const float ds = pr * (dp[c] - dl_r);
-                  const bool vis = full || (c < c_end && c <= c_hi && (c >= c_lo || c < c_sk));
-                  d2[h2] = vis ? ds : 0.f;
+                const float2 t = __ffma2_rn(make_float2(s[2 * e], s[2 * e + 1]), sl2v, nlse);
+                const float2 pr = make_float2(fast_exp2(t.x), fast_exp2(t.y));
+                float2 ds = __fmul2_rn(pr, __fadd2_rn(make_float2(dp[2 * e], dp[2 * e + 1]), ndl));
+                if (!full) {
+                  const int c = 2 * e;
+                  ds.x = (c < c_end && c <= c_hi && (c >= c_lo || c < c_sk)) ? ds.x : 0.f;
+                  ds.y = (c + 1 < c_end && c + 1 <= c_hi && (c + 1 >= c_lo || c + 1 < c_sk)) ? ds.y : 0.f;
                 }
-                dw[e] = Pack<T>::pack(d2[0], d2[1]);
+                dw[e] = Pack<T>::pack(ds.x, ds.y);
               }
               tmem_st8(tdS, dw);
             }

@@ -349,20 +349,23 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
             // query i = qc0 + c sees key j iff c >= c_min and (c < c_max or j < S)
             const int c_min = j - qc0;
             const int c_max = (W > 0 && j >= S) ? j + W - qc0 : (j < S ? 1 << 30 : -(1 << 30));
+            // two columns per step on the packed fp32 pipe (same roundings as the scalar
+            // fma / sub / mul)
+            const float2 sl2v = make_float2(sl2, sl2);
             uint32_t pw[8], dw[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              float pv[2], dv[2];
-#pragma unroll
-              for (int h2 = 0; h2 < 2; ++h2) {
-                const int c = 2 * e + h2;
-                float pr = fast_exp2(fmaf(s[c], sl2, -lse_s[c]));
-                if (!full) pr = (c >= c_min && c < c_max) ? pr : 0.f;
-                pv[h2] = pr;
-                dv[h2] = pr * (dp[c] - dl_s[c]);
+              const int c = 2 * e;
+              const float2 t = __ffma2_rn(make_float2(s[c], s[c + 1]), sl2v, make_float2(-lse_s[c], -lse_s[c + 1]));
+              float2 pr = make_float2(fast_exp2(t.x), fast_exp2(t.y));
+              if (!full) {
+                pr.x = (c >= c_min && c < c_max) ? pr.x : 0.f;
+                pr.y = (c + 1 >= c_min && c + 1 < c_max) ? pr.y : 0.f;
               }
-              pw[e] = Pack<T>::pack(pv[0], pv[1]);
-              dw[e] = Pack<T>::pack(dv[0], dv[1]);
+              const float2 dv = __fmul2_rn(pr, __fadd2_rn(make_float2(dp[c], dp[c + 1]),
+                                                          make_float2(-dl_s[c], -dl_s[c + 1])));
+              pw[e] = Pack<T>::pack(pr.x, pr.y);
+              dw[e] = Pack<T>::pack(dv.x, dv.y);
             }
             tmem_st8(tP, pw);
             tmem_st8(tdS, dw);
