@@ -219,6 +219,12 @@ int swa_selftest_wait_timeout(int limit_us, void* stream) {
                                                   static_cast<cudaStream_t>(stream)));
 }
 
+int swa_bwd_dkdv_launch_count(const SwaProblem* p) {
+  if (!p || check_problem(*p) != SWA_OK || (int64_t)p->batch * p->seq_len == 0) return 0;
+  const swa::SinkSplit ss = split_of(*p);
+  return 1 + (ss.fk_c > 0 ? 1 : 0) + (ss.nst > 0 ? 1 : 0);
+}
+
 size_t swa_bwd_workspace_size(const SwaProblem* p) {
   if (!p) return 0;
   if (check_problem(*p) != SWA_OK) return delta_bytes(*p);

@@ -51,8 +51,8 @@ class SwaPlan:
         self._ba = ctypes.byref(self.bwd_args)
         self.device = q.device
         self.launches = 0
-        # swa_bwd_dkdv launches a second (sink-row reduction) kernel when there are sinks
-        self._dkdv_kernels = 2 if min(int(sink_size), q.shape[2]) > 0 else 1
+        # swa_bwd_dkdv also launches the far sink-pair kernel and the sink-row reduction
+        self._dkdv_kernels = self.lib.swa_bwd_dkdv_launch_count(ctypes.byref(self.problem))
 
     def _s(self, stream) -> int:
         return (stream or torch.cuda.current_stream(self.device)).cuda_stream

@@ -101,6 +101,10 @@ SWA_API int swa_fwd(const SwaFwdArgs* args, void* stream);
 /* Scratch the backward needs (Delta rows and the sink-key partial sums), in bytes. */
 SWA_API size_t swa_bwd_workspace_size(const SwaProblem* p);
 
+/* Kernels swa_bwd_dkdv launches for this problem: the dK/dV kernel, plus the far sink-pair
+ * kernel and the sink-row reduction when there are sink keys (0 for an invalid problem). */
+SWA_API int swa_bwd_dkdv_launch_count(const SwaProblem* p);
+
 /* Full backward: dQ (which also writes Delta) then dK/dV.  Replaces
  * flash_attention_gpt_oss.py:397-435. */
 SWA_API int swa_bwd(const SwaBwdArgs* args, void* stream);

@@ -131,3 +131,18 @@ def test_no_alloc_rejects_problems_beyond_its_static_scratch():
     args = L.SwaBwdArgs(big, t, t, t, t, t, 1 << 20, t, t, t, None, 0)
     assert lib.swa_bwd_no_alloc(ctypes.byref(args), None) == L.SWA_ERR_TOO_LARGE
     assert lib.swa_bwd_no_alloc(None, None) == L.SWA_ERR_INVALID_ARG
+
+
+def test_dkdv_launch_count():
+    L = submodule("_lib")
+    lib = pkg().lib()
+    count = lambda **kw: lib.swa_bwd_dkdv_launch_count(ctypes.byref(_problem(**kw)))
+    # sinks seen from far past the window, D >= 64: dK/dV, far sink-pair kernel, reduction
+    assert count(n_q_heads=64, n_kv_heads=8, seq_len=4096, head_dim=64, window_size=128, sink_size=4) == 3
+    assert count(n_q_heads=64, n_kv_heads=8, seq_len=4096, head_dim=64, window_size=128, sink_size=0) == 1
+    # D = 32 keeps the far pairs as dK/dV items: dK/dV and the reduction
+    assert count(n_q_heads=8, n_kv_heads=8, seq_len=4096, head_dim=32, window_size=128, sink_size=4) == 2
+    # the window reaches every sink: no far pairs
+    assert count(n_q_heads=8, n_kv_heads=8, seq_len=256, head_dim=64, window_size=512, sink_size=4) == 2
+    assert count(head_dim=24) == 0
+    assert lib.swa_bwd_dkdv_launch_count(None) == 0
