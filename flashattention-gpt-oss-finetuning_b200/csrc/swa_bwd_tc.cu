@@ -450,13 +450,18 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
 
 // Sink rows: dK = scale * sum of partials, dV = sum, added in a fixed slot order
 // (deterministic).  One CTA per (batch, KV head, sink tile) and 32 consecutive outputs of its
-// {dK, dV} x sp x D block: each of the 8 warps sums a contiguous range of slots, and warp 0
-// adds the 8 range sums in order.
+// {dK, dV} x rows x D block (rows = the tile's sink keys, at most sp): each of the 16 warps
+// sums a contiguous range of slots, and warp 0 adds the 16 range sums in order.
+constexpr int kReduceWarps = 16;
+
+__host__ __device__ inline int reduce_rows(const BwdParams& p) { return p.S < p.sp ? p.S : p.sp; }
+
 template <typename T, int D>
-__global__ void __launch_bounds__(256) bwd_sink_reduce_kernel(BwdParams p) {
-  __shared__ float part_sum[8][32];
+__global__ void __launch_bounds__(32 * kReduceWarps) bwd_sink_reduce_kernel(BwdParams p) {
+  __shared__ float part_sum[kReduceWarps][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_out = 2 * p.sp * D;
+  const int rows = reduce_rows(p);
+  const int n_out = 2 * rows * D;
   const int n_oc = (n_out + 31) / 32;
   int rest = blockIdx.x;
   const int oc = rest % n_oc;
@@ -466,19 +471,20 @@ __global__ void __launch_bounds__(256) bwd_sink_reduce_kernel(BwdParams p) {
   const int kvh = rest % p.Hkv;
   const int b = rest / p.Hkv;
   const int o = oc * 32 + lane;
-  const int part = o / (p.sp * D);
-  const int r = (o / D) % p.sp;
+  const int part = o / (rows * D);
+  const int r = (o / D) % rows;
   const int d = o % D;
   const int j = kt * p.bn_split + r;
   const bool valid = o < n_out && j < p.S && j < p.L;
   SinkSplit ss;
   ss.bn = p.bn_split; ss.bm = p.bm_split; ss.ch = p.ch; ss.fk_c = p.fk_c; ss.fk_u = p.fk_u;
   const int n_slots = sink_slots(ss, kt, p.L, p.W, p.Hq / p.Hkv);
-  const int s_lo = n_slots * warp / 8, s_hi = n_slots * (warp + 1) / 8;
+  const int s_lo = n_slots * warp / kReduceWarps, s_hi = n_slots * (warp + 1) / kReduceWarps;
   float acc = 0.f;
   if (valid) {
     const int64_t stride = (int64_t)p.B * p.Hkv * p.nst * 2 * p.sp * D;
-    const float* src = p.part + (((int64_t)b * p.Hkv + kvh) * p.nst + kt) * 2 * p.sp * D + o;
+    const float* src = p.part + (((int64_t)b * p.Hkv + kvh) * p.nst + kt) * 2 * p.sp * D +
+                       ((int64_t)part * p.sp + r) * D + d;
 #pragma unroll 4
     for (int sl = s_lo; sl < s_hi; ++sl) acc += src[sl * stride];
   }
@@ -487,7 +493,7 @@ __global__ void __launch_bounds__(256) bwd_sink_reduce_kernel(BwdParams p) {
   if (warp != 0 || !valid) return;
   float v = 0.f;
 #pragma unroll
-  for (int w = 0; w < 8; ++w) v += part_sum[w][lane];
+  for (int w = 0; w < kReduceWarps; ++w) v += part_sum[w][lane];
   if (part == 0) {
     T* dk = static_cast<T*>(p.dk) + b * p.sdk.b + kvh * p.sdk.h + (int64_t)j * p.sdk.l + d;
     *dk = Pack<T>::from(v * p.scale);
@@ -499,9 +505,9 @@ __global__ void __launch_bounds__(256) bwd_sink_reduce_kernel(BwdParams p) {
 
 template <typename T, int D>
 cudaError_t launch_sink_reduce(const BwdParams& p, cudaStream_t st) {
-  const long long n = (long long)p.B * p.Hkv * p.nst * ((2 * p.sp * D + 31) / 32);
+  const long long n = (long long)p.B * p.Hkv * p.nst * ((2 * reduce_rows(p) * D + 31) / 32);
   if (n == 0) return cudaSuccess;
-  bwd_sink_reduce_kernel<T, D><<<(unsigned)n, 256, 0, st>>>(p);
+  bwd_sink_reduce_kernel<T, D><<<(unsigned)n, 32 * kReduceWarps, 0, st>>>(p);
   return cudaGetLastError();
 }
 
