@@ -205,7 +205,21 @@ def device_timed(w, dev, rank, steps, warmup):
     total_ms = start.elapsed_time(end)
     per_phase = {p: sum(evs[s][i].elapsed_time(evs[s][i + 1]) for s in range(steps)) / steps
                  for i, p in enumerate(phases)}
-    return total_ms, per_phase, plan.launches - launches0
+    launches = plan.launches - launches0
+    # the same step replayed from a CUDA graph (launch overhead out of the picture)
+    graph = plan.capture()
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    start.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    graph_ms = start.elapsed_time(end)
+    return total_ms, per_phase, launches, graph_ms
 
 
 def e2e_timed(w, dev, rank, steps, warmup):
@@ -303,7 +317,8 @@ def run_ours(args, w_job, rank, world, local_rank):
     clocks = ClockSampler(local_rank) if rank == 0 else None
     if clocks:
         clocks.start()
-    total_ms, per_phase, launches = device_timed(w, dev, rank, args.steps, args.warmup)
+    total_ms, per_phase, launches, graph_ms = device_timed(w, dev, rank, args.steps, args.warmup)
+    graph_ms = max_over_ranks(graph_ms, dev) / args.steps
     clk = clocks.stop() if clocks else None
     total_ms = max_over_ranks(total_ms, dev)
     ms = total_ms / args.steps
@@ -349,6 +364,8 @@ def run_ours(args, w_job, rank, world, local_rank):
                        l2="inputs larger than L2 (q, dO 134 MB each + k, v, o, grads)"),
         "phase_ms": per_phase,
         "gpu_launches": launches,
+        "cuda_graph": {"ms_per_step": graph_ms, "value": flops_job / (graph_ms * 1e-3) / 1e12,
+                       "note": "same step captured once (SwaPlan.capture) and replayed"},
         "roofline": roof,
         "clocks": clk,
         "e2e": e2e,

@@ -82,3 +82,20 @@ class SwaPlan:
         """One forward + backward over the bound buffers."""
         self.fwd(stream)
         self.bwd(stream)
+
+    def capture(self) -> "torch.cuda.CUDAGraph":
+        """Record one forward + backward (``step``) into a CUDA graph over the bound buffers.
+
+        The library allocates nothing and takes every pointer, size and TMA descriptor at
+        launch time, so the graph replays the same kernels on the same buffers: refill
+        ``q, k, v, dout`` in place and call ``replay()``.  The first ``step`` runs eagerly
+        before the capture (one-time kernel attribute set-up stays out of the graph)."""
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self.step(side)  # warm-up outside the graph
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.step()
+        return graph

@@ -230,3 +230,23 @@ def test_backward_from_a_fresh_host_thread():
     ref = orc.backward(q.float(), k.float(), v.float(), do.float(), 50, 4)
     for a, r in zip(out["grads"], ref[1:]):
         assert _rel(a, r) <= TOL[torch.float16]
+
+
+def test_cuda_graph_replay_matches_eager():
+    # one fwd + bwd captured once and replayed over refilled inputs
+    plan = submodule("plan")
+    dev = torch.device("cuda:0")
+    q, k, v, do = (t.to(dev) for t in rand((2, 8, 640, 64), (2, 2, 640, 64), torch.bfloat16, 91))
+    qb, kb, vb, dob = (t.clone() for t in (q, k, v, do))
+    p = plan.SwaPlan(qb, kb, vb, 128, 4, dout=dob)
+    g = p.capture()
+    for seed in (92, 93):
+        q2, k2, v2, do2 = (t.to(dev) for t in rand((2, 8, 640, 64), (2, 2, 640, 64), torch.bfloat16, seed))
+        for dst, src in zip((qb, kb, vb, dob), (q2, k2, v2, do2)):
+            dst.copy_(src)
+        g.replay()
+        torch.cuda.synchronize(dev)
+        assert_device_ok(dev)
+        ref = orc.backward(q2.float().cpu(), k2.float().cpu(), v2.float().cpu(), do2.float().cpu(), 128, 4)
+        for a, r in zip((p.o, p.dq, p.dk, p.dv), ref):
+            assert _rel(a, r) <= TOL[torch.bfloat16]
