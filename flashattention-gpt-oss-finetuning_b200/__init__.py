@@ -3,9 +3,10 @@
 Drop-in for the reference's ``flash_attention_gpt_oss`` entry points; the compute runs in the
 C-ABI library ``lib/libswa_attn.so`` (``include/swa_attn.h``).
 """
-from .flash_attention_gpt_oss import (FlashSWDAWithSink, flash_swda_with_sink, swa_backward,
+from .flash_attention_gpt_oss import (FlashSWDAWithSink, FlashSWDAWithSinkLogits,
+                                      flash_swda_with_sink, swa_backward,
                                       swa_forward)
 from ._lib import SwaDeviceTimeout, SwaError, lib, lib_path
 
-__all__ = ["FlashSWDAWithSink", "flash_swda_with_sink", "swa_forward", "swa_backward",
+__all__ = ["FlashSWDAWithSink", "FlashSWDAWithSinkLogits", "flash_swda_with_sink", "swa_forward", "swa_backward",
            "SwaError", "SwaDeviceTimeout", "lib", "lib_path"]

@@ -29,7 +29,7 @@ EXPORTED_SYMBOLS = (
     "swa_fwd", "swa_bwd", "swa_bwd_preprocess", "swa_bwd_dq", "swa_bwd_dkdv",
     "swa_bwd_workspace_size", "swa_bwd_dkdv_launch_count", "swa_bwd_no_alloc", "swa_check_device",
     "swa_status_string", "swa_last_cuda_error", "swa_version", "swa_lse_row_stride",
-    "swa_selftest_wait_timeout",
+    "swa_selftest_wait_timeout", "swa_fwd_sink_logits", "swa_bwd_sink_logits",
 )
 
 
@@ -92,6 +92,11 @@ def _declare(l):
         getattr(l, name).argtypes = [P(SwaBwdArgs), ctypes.c_void_p]
         getattr(l, name).restype = ctypes.c_int
     l.swa_fwd.restype = ctypes.c_int
+    l.swa_fwd_sink_logits.argtypes = [P(SwaFwdArgs), ctypes.c_void_p, ctypes.c_void_p]
+    l.swa_fwd_sink_logits.restype = ctypes.c_int
+    l.swa_bwd_sink_logits.argtypes = [P(SwaBwdArgs), ctypes.c_void_p, ctypes.c_void_p,
+                                      ctypes.c_void_p]
+    l.swa_bwd_sink_logits.restype = ctypes.c_int
     l.swa_bwd_workspace_size.argtypes = [P(SwaProblem)]
     l.swa_bwd_workspace_size.restype = ctypes.c_size_t
     l.swa_bwd_dkdv_launch_count.argtypes = [P(SwaProblem)]

@@ -12,6 +12,8 @@
 namespace swa {
 template <typename T, int D> cudaError_t launch_fwd_tc(const FwdParams&, cudaStream_t, int*);
 cudaError_t launch_selftest_wait_timeout(int* err, unsigned long long limit_ns, cudaStream_t st);
+cudaError_t launch_sink_logit_grad(const float* lse, const float* delta, const float* sinks,
+                                   float* dsinks, int B, int Hq, int lse_ld, cudaStream_t st);
 template <typename T, int D> cudaError_t launch_bwd_preprocess(const BwdParams&, cudaStream_t);
 template <typename T, int D> cudaError_t launch_bwd_dq_tc(const BwdParams&, cudaStream_t, int*);
 template <typename T, int D> cudaError_t launch_bwd_dkdv_tc(const BwdParams&, cudaStream_t, int*);
@@ -231,7 +233,9 @@ size_t swa_bwd_workspace_size(const SwaProblem* p) {
   return delta_bytes(*p) + partial_bytes(*p);
 }
 
-int swa_fwd(const SwaFwdArgs* a, void* stream) {
+namespace {
+
+int fwd_impl(const SwaFwdArgs* a, const float* sinks, void* stream) {
   if (!a) return SWA_ERR_INVALID_ARG;
   int st = check_problem(a->p);
   if (st) return st;
@@ -248,7 +252,17 @@ int swa_fwd(const SwaFwdArgs* a, void* stream) {
   kp.B = a->p.batch; kp.Hq = a->p.n_q_heads; kp.Hkv = a->p.n_kv_heads; kp.L = a->p.seq_len;
   kp.W = effective_window(a->p.window_size, a->p.seq_len); kp.S = a->p.sink_size;
   kp.scale_log2 = a->p.softmax_scale * swa::kLog2e;
+  kp.sinks = sinks;
   return dispatch<Fwd>(a->p, kp, static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+
+int swa_fwd(const SwaFwdArgs* a, void* stream) { return fwd_impl(a, nullptr, stream); }
+
+int swa_fwd_sink_logits(const SwaFwdArgs* a, const float* sink_logits, void* stream) {
+  if (!sink_logits) return SWA_ERR_INVALID_ARG;
+  return fwd_impl(a, sink_logits, stream);
 }
 
 int swa_bwd_preprocess(const SwaBwdArgs* a, void* stream) {
@@ -280,6 +294,23 @@ int swa_bwd(const SwaBwdArgs* a, void* stream) {
   // the dQ pass also computes Delta = rowsum(dO * O) into the workspace for the dK/dV pass
   if ((st = dispatch<Dq>(a->p, kp, s))) return st;
   return dispatch<Dkdv>(a->p, kp, s);
+}
+
+int swa_bwd_sink_logits(const SwaBwdArgs* a, const float* sink_logits, float* dsink_logits,
+                        void* stream) {
+  if (!a || !sink_logits || !dsink_logits) return SWA_ERR_INVALID_ARG;
+  swa::BwdParams kp;
+  int st = build_bwd(a, &kp);
+  if (st) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((int64_t)a->p.batch * a->p.seq_len != 0) {
+    // the keys' gradients need no change: lse already holds the sink in each row's normaliser
+    if ((st = dispatch<Dq>(a->p, kp, s))) return st;
+    if ((st = dispatch<Dkdv>(a->p, kp, s))) return st;
+  }
+  const bool empty = (int64_t)a->p.batch * a->p.seq_len == 0;
+  return record(swa::launch_sink_logit_grad(a->lse, kp.delta, sink_logits, dsink_logits,
+                                            empty ? 0 : a->p.batch, a->p.n_q_heads, kp.lse_ld, s));
 }
 
 }  // extern "C"

@@ -404,7 +404,18 @@ __global__ void __launch_bounds__(224, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
       // O goes through the swizzled staging tile and one TMA store (rows past L are clipped).
       const bool have_o = n > 0 && ok;
       const float l = rs.l;
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      float inv = l > 0.f ? 1.f / l : 0.f;
+      float lse2 = l > 0.f ? rs.m_used + __log2f(l) : -INFINITY;
+      if (p.sinks != nullptr) {
+        // learned sink logit: one more softmax column of value 0, so the row's normaliser
+        // becomes 2^lse2 + 2^s2 and O = acc * 2^(m - lse2')
+        const float s2 = p.sinks[h] * kLog2e;
+        if (s2 > -INFINITY) {
+          const float mx = fmaxf(lse2, s2);
+          lse2 = mx + log2f(exp2f(lse2 - mx) + exp2f(s2 - mx));
+          inv = l > 0.f ? exp2f(rs.m_used - lse2) : 0.f;
+        }
+      }
       if (threadIdx.x == 64) bulk_wait_read_all();  // the previous item's store has read Ost
       named_bar_sync(1, 128);
       constexpr uint32_t SWM = C::ROWB / 16 - 1;
@@ -439,7 +450,7 @@ __global__ void __launch_bounds__(224, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
         bulk_commit();
       }
       if (i < L)
-        p.lse[((int64_t)b * Hq + h) * p.lse_ld + i] = l > 0.f ? rs.m_used + __log2f(l) : -INFINITY;
+        p.lse[((int64_t)b * Hq + h) * p.lse_ld + i] = lse2;
       else if (i < p.lse_ld)
         p.lse[((int64_t)b * Hq + h) * p.lse_ld + i] = INFINITY;
       if (have_o) {

@@ -19,6 +19,7 @@ struct FwdParams {
   float scale_log2;  // softmax_scale * log2(e)
   int sink_box;      // keys per sink segment (tensor-core forward)
   int lse_ld;        // row stride of lse (L rounded up to 64)
+  const float* sinks;  // [Hq] learned sink logits (natural log units), or nullptr for none
 };
 
 struct BwdParams {

@@ -96,11 +96,26 @@ def _validate(q, k, v, is_causal):
         raise ValueError("q, k, v must be on the same CUDA device")
 
 
+def _sink_logits_f32(sinks: torch.Tensor, q: torch.Tensor) -> torch.Tensor:
+    """Learned sink logits as the contiguous fp32 [Hq] device array the library reads."""
+    if not isinstance(sinks, torch.Tensor) or sinks.numel() != q.shape[1] or sinks.dim() != 1:
+        raise ValueError(f"sinks must be a 1-D tensor of {q.shape[1]} (query heads) logits")
+    if sinks.device != q.device:
+        raise ValueError("sinks must be on the device of q")
+    return sinks.detach().to(torch.float32).contiguous()
+
+
 def swa_forward(q, k, v, window_size: int, sink_size: int = 0,
-                softmax_scale: Optional[float] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+                softmax_scale: Optional[float] = None,
+                sink_logits: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Forward only: returns ``(o, lse)`` where ``lse`` is the base-2 row log-sum-exp
     ([B, Hq, L] fp32 view of a buffer whose rows are padded to a multiple of 64; -inf for a
-    row that sees no key).  Pass it unchanged to :func:`swa_backward`."""
+    row that sees no key).  Pass it unchanged to :func:`swa_backward`.
+
+    ``sink_logits`` ([Hq], natural-log units, not scaled by ``softmax_scale``): learned
+    per-head sink logits, GPT-OSS's form, an additional mode beside the reference's sink
+    tokens.  Each row's softmax gets one more column of that value with no value vector;
+    ``lse`` then includes it."""
     _validate(q, k, v, True)
     d = q.shape[-1]
     if softmax_scale is None:
@@ -113,15 +128,23 @@ def swa_forward(q, k, v, window_size: int, sink_size: int = 0,
     args = _lib.SwaFwdArgs(_problem(q, k, window_size, sink_size, softmax_scale, dk_),
                            _tensor(qp), _tensor(kp), _tensor(vp), _tensor(o), lse.data_ptr())
     with torch.cuda.device(q.device):
-        _lib.check(_lib.lib().swa_fwd(ctypes.byref(args), _stream(q.device)), "swa_fwd")
+        if sink_logits is None:
+            _lib.check(_lib.lib().swa_fwd(ctypes.byref(args), _stream(q.device)), "swa_fwd")
+        else:
+            sl = _sink_logits_f32(sink_logits, q)
+            _lib.check(_lib.lib().swa_fwd_sink_logits(ctypes.byref(args), sl.data_ptr(),
+                                                      _stream(q.device)), "swa_fwd_sink_logits")
     if dk_ != d:
         o = o[..., :d]
     return o, lse[..., :l]
 
 
 def swa_backward(q, k, v, o, lse, do, window_size: int, sink_size: int = 0,
-                 softmax_scale: Optional[float] = None):
-    """Backward: returns ``(dq, dk, dv)`` in the input dtype (deterministic)."""
+                 softmax_scale: Optional[float] = None,
+                 sink_logits: Optional[torch.Tensor] = None):
+    """Backward: returns ``(dq, dk, dv)`` in the input dtype (deterministic).  With
+    ``sink_logits`` (the forward's), returns ``(dq, dk, dv, dsink_logits)``, the last one
+    fp32 [Hq]."""
     d = q.shape[-1]
     if softmax_scale is None:
         softmax_scale = 1.0 / math.sqrt(d)
@@ -141,11 +164,18 @@ def swa_backward(q, k, v, o, lse, do, window_size: int, sink_size: int = 0,
     args = _lib.SwaBwdArgs(prob, _tensor(qp), _tensor(kp), _tensor(vp), _tensor(op), _tensor(dop),
                            lse.data_ptr(), _tensor(dq), _tensor(dk), _tensor(dv),
                            ws.data_ptr(), ws_bytes)
+    dsl = None
     with torch.cuda.device(q.device):
-        _lib.check(lib.swa_bwd(ctypes.byref(args), _stream(q.device)), "swa_bwd")
+        if sink_logits is None:
+            _lib.check(lib.swa_bwd(ctypes.byref(args), _stream(q.device)), "swa_bwd")
+        else:
+            sl = _sink_logits_f32(sink_logits, q)
+            dsl = torch.empty_like(sl)
+            _lib.check(lib.swa_bwd_sink_logits(ctypes.byref(args), sl.data_ptr(), dsl.data_ptr(),
+                                               _stream(q.device)), "swa_bwd_sink_logits")
     if dk_ != d:
         dq, dk, dv = dq[..., :d], dk[..., :d], dv[..., :d]
-    return dq, dk, dv
+    return (dq, dk, dv) if dsl is None else (dq, dk, dv, dsl)
 
 
 class FlashSWDAWithSink(torch.autograd.Function):
@@ -171,7 +201,36 @@ class FlashSWDAWithSink(torch.autograd.Function):
         return dq, dk, dv, None, None, None, None
 
 
+class FlashSWDAWithSinkLogits(torch.autograd.Function):
+    """FlashSWDAWithSink plus learned per-head sink logits (GPT-OSS's form of attention
+    sinks; no counterpart in the reference).  ``sinks``: [Hq] logits, natural-log units, not
+    scaled by ``softmax_scale``; gets a gradient in its own dtype."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, sinks, window_size, sink_size, is_causal=True, softmax_scale=None):
+        _validate(q, k, v, is_causal)
+        if softmax_scale is None:
+            softmax_scale = 1.0 / math.sqrt(q.shape[-1])
+        o, lse = swa_forward(q, k, v, window_size, sink_size, softmax_scale, sink_logits=sinks)
+        ctx.save_for_backward(q, k, v, o, lse, sinks)
+        ctx.softmax_scale = softmax_scale
+        ctx.window_size = window_size
+        ctx.sink_size = sink_size
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse, sinks = ctx.saved_tensors
+        dq, dk, dv, dsl = swa_backward(q, k, v, o, lse, do, ctx.window_size, ctx.sink_size,
+                                       ctx.softmax_scale, sink_logits=sinks)
+        return dq, dk, dv, dsl.to(sinks.dtype), None, None, None, None
+
+
 def flash_swda_with_sink(q, k, v, window_size: int, sink_size: int = 0, is_causal: bool = True,
-                         scale: Optional[float] = None):
-    """Same signature as the reference (flash_attention_gpt_oss.py:437-438)."""
+                         scale: Optional[float] = None, sinks: Optional[torch.Tensor] = None):
+    """Same signature as the reference (flash_attention_gpt_oss.py:437-438), plus the
+    optional keyword ``sinks`` ([Hq] learned sink logits, see FlashSWDAWithSinkLogits)."""
+    if sinks is not None:
+        return FlashSWDAWithSinkLogits.apply(q, k, v, sinks, window_size, sink_size, is_causal,
+                                             scale)
     return FlashSWDAWithSink.apply(q, k, v, window_size, sink_size, is_causal, scale)

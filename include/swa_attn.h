@@ -122,6 +122,22 @@ SWA_API int swa_bwd_dq(const SwaBwdArgs* args, void* stream);
  * flash_attention_gpt_oss.py:295-304, 323-332. */
 SWA_API int swa_bwd_dkdv(const SwaBwdArgs* args, void* stream);
 
+/* Learned per-head sink logits: an additional mode with no counterpart in the reference
+ * (whose sinks are the first sink_size key tokens; both can be combined).  This is the form
+ * GPT-OSS itself uses: query head h has a learned logit sink_logits[h] (fp32 device array of
+ * n_q_heads values, natural-log units, NOT multiplied by softmax_scale) that joins every
+ * row's softmax as one more column with no value vector:
+ *   P = softmax([scale * q k^T (masked), sink_logits[h]]),  o = P[:, :L] v.
+ * -inf means no sink for that head.  lse then includes the sink column, so a row that sees
+ * no key has o = 0 and lse = log2(e) * sink_logits[h]. */
+SWA_API int swa_fwd_sink_logits(const SwaFwdArgs* args, const float* sink_logits, void* stream);
+
+/* Backward of swa_fwd_sink_logits (its o and lse): dq, dk, dv as swa_bwd, plus
+ * dsink_logits[h] = d loss / d sink_logits[h] = -sum_{b,i} P_sink[b,h,i] * Delta[b,h,i]
+ * (fp32 device array of n_q_heads values, overwritten; deterministic). */
+SWA_API int swa_bwd_sink_logits(const SwaBwdArgs* args, const float* sink_logits,
+                                float* dsink_logits, void* stream);
+
 /* Backward that allocates nothing and takes no workspace.  No counterpart in the reference.
  *
  * For callers that cannot call cudaMalloc: a host that hands this library only its tensors

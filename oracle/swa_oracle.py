@@ -204,3 +204,46 @@ def rows_backward(qh, kh, vh, doh, r0: int, r1: int, window_size: int, sink_size
     ds = p * (do @ v.transpose(-1, -2) - delta)
     dq = (ds @ k) * sc
     return o, dq, keys_t, p, ds
+
+
+# ---------------------------------------------------------------------------------------
+# Learned per-head sink logits (an additional mode; not part of the reference).
+#
+# The form GPT-OSS uses: each query head h has a learned logit sink_h that joins every row's
+# softmax as one more column with value 0 -- P = softmax([scale q k^T (masked), sink_h]),
+# O = P[:, :-1] V.  Restated here from that published formula; the gradients come from
+# autograd on this float64 restatement, including d loss / d sink_h = -sum_i P_i,sink Delta_i.
+# It combines with the token sinks (sink_size) of the reference's mask.
+# ---------------------------------------------------------------------------------------
+
+def _sink_logit_attention(q, k, v, window_size, sink_size, sinks, scale):
+    b, hq, l, d = q.shape
+    ke, ve = _expand_kv(k, hq), _expand_kv(v, hq)
+    mask = visible_mask(l, window_size, sink_size)
+    s = (q @ ke.transpose(-1, -2)) * _scale(d, scale)
+    s = s.masked_fill(~mask, float("-inf"))
+    col = sinks.reshape(1, hq, 1, 1).expand(b, hq, l, 1)
+    p = torch.softmax(torch.cat([s, col], dim=-1), dim=-1)
+    lse = torch.logsumexp(torch.cat([s, col], dim=-1), dim=-1)
+    return p[..., :l] @ ve, lse
+
+
+def forward_sink_logits(q, k, v, window_size: int, sink_size: int, sinks, scale: Optional[float] = None,
+                        compute_dtype=torch.float64):
+    """(o, lse) with the learned sink logits ``sinks`` ([Hq], natural-log units)."""
+    q, k, v = (t.detach().to("cpu", compute_dtype) for t in (q, k, v))
+    sinks = torch.as_tensor(sinks).detach().to("cpu", compute_dtype)
+    with torch.no_grad():
+        return _sink_logit_attention(q, k, v, window_size, sink_size, sinks, scale)
+
+
+def backward_sink_logits(q, k, v, do, window_size: int, sink_size: int, sinks,
+                         scale: Optional[float] = None, compute_dtype=torch.float64):
+    """(o, dq, dk, dv, dsinks) for loss = <O, dO> with learned sink logits."""
+    q, k, v, do = (t.detach().to("cpu", compute_dtype).requires_grad_(r)
+                   for t, r in zip((q, k, v, do), (True, True, True, False)))
+    sinks = torch.as_tensor(sinks).detach().to("cpu", compute_dtype).requires_grad_(True)
+    with torch.enable_grad():
+        o, _ = _sink_logit_attention(q, k, v, window_size, sink_size, sinks, scale)
+        (o * do).sum().backward()
+    return o.detach(), q.grad, k.grad, v.grad, sinks.grad

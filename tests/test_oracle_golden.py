@@ -58,3 +58,23 @@ def test_useful_pairs_closed_form():
         assert int(m.sum()) == orc.visible_pairs_per_head(l, w, s)
     # published accounting: config 2 has 136,198,656 useful pairs
     assert 4 * 64 * orc.visible_pairs_per_head(4096, 128, 4) == 136198656
+
+
+def test_sink_logits_oracle_reduces_to_token_sinks():
+    # a sink logit of -inf is no sink at all; a finite one only rescales each row's weights
+    g = torch.Generator().manual_seed(3)
+    q, k, v, do = (torch.randn(s, generator=g, dtype=torch.float64)
+                   for s in ((1, 4, 70, 16), (1, 2, 70, 16), (1, 2, 70, 16), (1, 4, 70, 16)))
+    o0, dq0, dk0, dv0 = orc.backward(q, k, v, do, 20, 3)
+    o1, dq1, dk1, dv1, ds1 = orc.backward_sink_logits(q, k, v, do, 20, 3, torch.full((4,), -float("inf")))
+    for a, b in zip((o0, dq0, dk0, dv0), (o1, dq1, dk1, dv1)):
+        assert torch.allclose(a, b, atol=1e-12)
+    sinks = torch.tensor([-1.0, 0.0, 0.5, 2.0], dtype=torch.float64)
+    o2, _, _, _, ds2 = orc.backward_sink_logits(q, k, v, do, 20, 3, sinks)
+    _, lse0 = orc.forward(q, k, v, 20, 3)
+    w = 1.0 / (1.0 + torch.exp(sinks.reshape(1, 4, 1) - lse0))   # share kept by the keys
+    assert torch.allclose(o2, o0 * w[..., None], atol=1e-12)
+    # d loss / d sink_h = -sum_i P_i,sink Delta_i with Delta_i = rowsum(dO * O)
+    p_sink = torch.exp(sinks.reshape(1, 4, 1) - torch.logaddexp(lse0, sinks.reshape(1, 4, 1)))
+    delta = (do * o2).sum(-1)
+    assert torch.allclose(ds2, -(p_sink * delta).sum((0, 2)), atol=1e-10)
