@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "swa_bwd_workspace_size", "swa_bwd_dkdv_launch_count", "swa_bwd_no_alloc", "swa_check_device",
     "swa_status_string", "swa_last_cuda_error", "swa_version", "swa_lse_row_stride",
     "swa_selftest_wait_timeout", "swa_fwd_sink_logits", "swa_bwd_sink_logits",
+    "swa_varlen_lse_floats", "swa_varlen_bwd_workspace_size", "swa_varlen_fwd", "swa_varlen_bwd",
 )
 
 
@@ -56,6 +57,25 @@ class SwaBwdArgs(ctypes.Structure):
                 ("o", SwaTensor), ("dout", SwaTensor), ("lse", ctypes.c_void_p),
                 ("dq", SwaTensor), ("dk", SwaTensor), ("dv", SwaTensor),
                 ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t)]
+
+
+class SwaPackedTensor(ctypes.Structure):
+    _fields_ = [("ptr", ctypes.c_void_p), ("stride_t", ctypes.c_int64), ("stride_h", ctypes.c_int64)]
+
+
+class SwaVarlenFwdArgs(ctypes.Structure):
+    _fields_ = [("p", SwaProblem), ("cu_seqlens", ctypes.c_void_p), ("q", SwaPackedTensor),
+                ("k", SwaPackedTensor), ("v", SwaPackedTensor), ("o", SwaPackedTensor),
+                ("lse", ctypes.c_void_p), ("sink_logits", ctypes.c_void_p)]
+
+
+class SwaVarlenBwdArgs(ctypes.Structure):
+    _fields_ = [("p", SwaProblem), ("cu_seqlens", ctypes.c_void_p), ("q", SwaPackedTensor),
+                ("k", SwaPackedTensor), ("v", SwaPackedTensor), ("o", SwaPackedTensor),
+                ("dout", SwaPackedTensor), ("lse", ctypes.c_void_p), ("dq", SwaPackedTensor),
+                ("dk", SwaPackedTensor), ("dv", SwaPackedTensor), ("sink_logits", ctypes.c_void_p),
+                ("dsink_logits", ctypes.c_void_p), ("workspace", ctypes.c_void_p),
+                ("workspace_bytes", ctypes.c_size_t)]
 
 
 class SwaError(RuntimeError):
@@ -97,6 +117,13 @@ def _declare(l):
     l.swa_bwd_sink_logits.argtypes = [P(SwaBwdArgs), ctypes.c_void_p, ctypes.c_void_p,
                                       ctypes.c_void_p]
     l.swa_bwd_sink_logits.restype = ctypes.c_int
+    for name in ("swa_varlen_lse_floats", "swa_varlen_bwd_workspace_size"):
+        getattr(l, name).argtypes = [P(SwaProblem), ctypes.c_void_p]
+        getattr(l, name).restype = ctypes.c_size_t
+    l.swa_varlen_fwd.argtypes = [P(SwaVarlenFwdArgs), ctypes.c_void_p]
+    l.swa_varlen_fwd.restype = ctypes.c_int
+    l.swa_varlen_bwd.argtypes = [P(SwaVarlenBwdArgs), ctypes.c_void_p]
+    l.swa_varlen_bwd.restype = ctypes.c_int
     l.swa_bwd_workspace_size.argtypes = [P(SwaProblem)]
     l.swa_bwd_workspace_size.restype = ctypes.c_size_t
     l.swa_bwd_dkdv_launch_count.argtypes = [P(SwaProblem)]

@@ -13,7 +13,8 @@ namespace swa {
 template <typename T, int D> cudaError_t launch_fwd_tc(const FwdParams&, cudaStream_t, int*);
 cudaError_t launch_selftest_wait_timeout(int* err, unsigned long long limit_ns, cudaStream_t st);
 cudaError_t launch_sink_logit_grad(const float* lse, const float* delta, const float* sinks,
-                                   float* dsinks, int B, int Hq, int lse_ld, cudaStream_t st);
+                                   float* dsinks, int B, int Hq, int lse_ld, bool accumulate,
+                                   cudaStream_t st);
 template <typename T, int D> cudaError_t launch_bwd_preprocess(const BwdParams&, cudaStream_t);
 template <typename T, int D> cudaError_t launch_bwd_dq_tc(const BwdParams&, cudaStream_t, int*);
 template <typename T, int D> cudaError_t launch_bwd_dkdv_tc(const BwdParams&, cudaStream_t, int*);
@@ -310,7 +311,141 @@ int swa_bwd_sink_logits(const SwaBwdArgs* a, const float* sink_logits, float* ds
   }
   const bool empty = (int64_t)a->p.batch * a->p.seq_len == 0;
   return record(swa::launch_sink_logit_grad(a->lse, kp.delta, sink_logits, dsink_logits,
-                                            empty ? 0 : a->p.batch, a->p.n_q_heads, kp.lse_ld, s));
+                                            empty ? 0 : a->p.batch, a->p.n_q_heads, kp.lse_ld,
+                                            false, s));
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// Variable-length (packed) batches: each sequence is a one-sequence dense problem whose
+// tensors are views into the packed buffers (token stride = the dense row stride).
+// ---------------------------------------------------------------------------------------
+namespace {
+
+// cu_seqlens: batch + 1 offsets, starting at 0, non-decreasing.
+int check_cu(const SwaProblem* p, const int32_t* cu) {
+  if (!p || !cu) return SWA_ERR_INVALID_ARG;
+  if (p->batch < 0 || cu[0] != 0) return SWA_ERR_INVALID_ARG;
+  for (int b = 0; b < p->batch; ++b)
+    if (cu[b + 1] < cu[b]) return SWA_ERR_INVALID_ARG;
+  return SWA_OK;
+}
+
+SwaProblem seq_problem(const SwaProblem& p, int L) {
+  SwaProblem q = p;
+  q.batch = 1;
+  q.seq_len = L;
+  return q;
+}
+
+// View of sequence rows [t0, ...) of a packed tensor as a [1, H, L, D] dense tensor.
+SwaTensor seq_view(const SwaPackedTensor& t, int64_t t0) {
+  SwaTensor r;
+  r.ptr = t.ptr ? static_cast<void*>(static_cast<char*>(t.ptr) + t0 * t.stride_t * 2) : nullptr;
+  r.stride_b = 0;
+  r.stride_h = t.stride_h;
+  r.stride_l = t.stride_t;
+  return r;
+}
+
+bool packed_ok(const SwaPackedTensor& t) {
+  return t.ptr && t.stride_t >= 0 && t.stride_h >= 0 && t.stride_t % 8 == 0 && t.stride_h % 8 == 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t swa_varlen_lse_floats(const SwaProblem* p, const int32_t* cu) {
+  if (check_cu(p, cu) != SWA_OK || p->n_q_heads <= 0) return 0;
+  size_t n = 0;
+  for (int b = 0; b < p->batch; ++b) n += (size_t)swa::stat_row_stride(cu[b + 1] - cu[b]);
+  return n * (size_t)p->n_q_heads;
+}
+
+size_t swa_varlen_bwd_workspace_size(const SwaProblem* p, const int32_t* cu) {
+  if (check_cu(p, cu) != SWA_OK) return 0;
+  size_t m = 0;
+  for (int b = 0; b < p->batch; ++b) {
+    const SwaProblem q = seq_problem(*p, cu[b + 1] - cu[b]);
+    const size_t w = swa_bwd_workspace_size(&q);
+    m = w > m ? w : m;
+  }
+  return m;
+}
+
+int swa_varlen_fwd(const SwaVarlenFwdArgs* a, void* stream) {
+  if (!a) return SWA_ERR_INVALID_ARG;
+  int st = check_cu(&a->p, a->cu_seqlens);
+  if (st) return st;
+  if ((st = check_problem(seq_problem(a->p, 0)))) return st;
+  const int32_t* cu = a->cu_seqlens;
+  if (cu[a->p.batch] == 0) return SWA_OK;
+  const SwaPackedTensor* need[] = {&a->q, &a->k, &a->v, &a->o};
+  for (const SwaPackedTensor* t : need)
+    if (!packed_ok(*t)) return SWA_ERR_INVALID_ARG;
+  if (!a->lse) return SWA_ERR_INVALID_ARG;
+  size_t lse_off = 0;
+  for (int b = 0; b < a->p.batch; ++b) {
+    const int L = cu[b + 1] - cu[b];
+    if (L == 0) continue;
+    SwaFwdArgs f;
+    f.p = seq_problem(a->p, L);
+    f.q = seq_view(a->q, cu[b]); f.k = seq_view(a->k, cu[b]);
+    f.v = seq_view(a->v, cu[b]); f.o = seq_view(a->o, cu[b]);
+    f.lse = a->lse + lse_off;
+    if ((st = fwd_impl(&f, a->sink_logits, stream))) return st;
+    lse_off += (size_t)a->p.n_q_heads * swa::stat_row_stride(L);
+  }
+  return SWA_OK;
+}
+
+int swa_varlen_bwd(const SwaVarlenBwdArgs* a, void* stream) {
+  if (!a) return SWA_ERR_INVALID_ARG;
+  int st = check_cu(&a->p, a->cu_seqlens);
+  if (st) return st;
+  if ((st = check_problem(seq_problem(a->p, 0)))) return st;
+  if (a->sink_logits && !a->dsink_logits) return SWA_ERR_INVALID_ARG;
+  const int32_t* cu = a->cu_seqlens;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  bool wrote_dsinks = false;
+  if (cu[a->p.batch] > 0) {
+    const SwaPackedTensor* need[] = {&a->q, &a->k, &a->v, &a->o, &a->dout, &a->dq, &a->dk, &a->dv};
+    for (const SwaPackedTensor* t : need)
+      if (!packed_ok(*t)) return SWA_ERR_INVALID_ARG;
+    if (!a->lse) return SWA_ERR_INVALID_ARG;
+    if (a->workspace_bytes < swa_varlen_bwd_workspace_size(&a->p, cu)) return SWA_ERR_WORKSPACE;
+    size_t lse_off = 0;
+    for (int b = 0; b < a->p.batch; ++b) {
+      const int L = cu[b + 1] - cu[b];
+      if (L == 0) continue;
+      SwaBwdArgs g;
+      g.p = seq_problem(a->p, L);
+      g.q = seq_view(a->q, cu[b]); g.k = seq_view(a->k, cu[b]); g.v = seq_view(a->v, cu[b]);
+      g.o = seq_view(a->o, cu[b]); g.dout = seq_view(a->dout, cu[b]);
+      g.dq = seq_view(a->dq, cu[b]); g.dk = seq_view(a->dk, cu[b]); g.dv = seq_view(a->dv, cu[b]);
+      g.lse = a->lse + lse_off;
+      g.workspace = a->workspace;           // reused in stream order, one sequence at a time
+      g.workspace_bytes = a->workspace_bytes;
+      swa::BwdParams kp;
+      if ((st = build_bwd(&g, &kp))) return st;
+      if ((st = dispatch<Dq>(g.p, kp, s))) return st;
+      if ((st = dispatch<Dkdv>(g.p, kp, s))) return st;
+      if (a->sink_logits) {
+        if ((st = record(swa::launch_sink_logit_grad(g.lse, kp.delta, a->sink_logits,
+                                                     a->dsink_logits, 1, a->p.n_q_heads,
+                                                     kp.lse_ld, wrote_dsinks, s))))
+          return st;
+        wrote_dsinks = true;
+      }
+      lse_off += (size_t)a->p.n_q_heads * swa::stat_row_stride(L);
+    }
+  }
+  if (a->sink_logits && !wrote_dsinks)  // no tokens at all: d sink = 0
+    return record(swa::launch_sink_logit_grad(nullptr, nullptr, a->sink_logits, a->dsink_logits,
+                                              0, a->p.n_q_heads, 0, false, s));
+  return SWA_OK;
 }
 
 }  // extern "C"

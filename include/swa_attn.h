@@ -138,6 +138,60 @@ SWA_API int swa_fwd_sink_logits(const SwaFwdArgs* args, const float* sink_logits
 SWA_API int swa_bwd_sink_logits(const SwaBwdArgs* args, const float* sink_logits,
                                 float* dsink_logits, void* stream);
 
+/* ------------------------------------------------------------------------------------
+ * Variable-length (packed) batches: an additional mode with no counterpart in the reference
+ * (which takes dense [B, H, L, D] only, flash_attention_gpt_oss.py:348).  `batch` sequences
+ * of different lengths are packed along one token axis: q, o, dout, dq are [T, Hq, D] and
+ * k, v, dk, dv are [T, Hkv, D] (T = cu_seqlens[batch]); sequence b holds tokens
+ * [cu_seqlens[b], cu_seqlens[b+1]) and attends only inside itself, with the usual mask in
+ * its own positions (key j visible to query i iff j <= i and (i - j < W or j < S), i and j
+ * counted from the sequence's first token).  cu_seqlens is a HOST array of batch + 1
+ * non-decreasing int32 offsets starting at 0.  SwaProblem.seq_len is ignored.
+ * lse: n_q_heads * swa_varlen_lse_floats(...) fp32; sequence b owns a [Hq, round_up(L_b, 64)]
+ * block after those of sequences 0..b-1.  Every sequence runs the dense kernels as a
+ * one-sequence problem on `stream`, in order.
+ * ------------------------------------------------------------------------------------ */
+
+/* A packed [T, H, D] tensor: device pointer + element strides of the token and head dims. */
+typedef struct SwaPackedTensor {
+  void* ptr;
+  int64_t stride_t, stride_h;
+} SwaPackedTensor;
+
+typedef struct SwaVarlenFwdArgs {
+  SwaProblem p;                /* batch = number of sequences; seq_len ignored            */
+  const int32_t* cu_seqlens;   /* host, batch + 1 entries                                 */
+  SwaPackedTensor q, k, v;     /* inputs                                                  */
+  SwaPackedTensor o;           /* output [T, Hq, D]                                       */
+  float* lse;                  /* output, swa_varlen_lse_floats(&p, cu_seqlens) floats    */
+  const float* sink_logits;    /* optional [Hq] learned sink logits (see swa_fwd_sink_logits) */
+} SwaVarlenFwdArgs;
+
+typedef struct SwaVarlenBwdArgs {
+  SwaProblem p;
+  const int32_t* cu_seqlens;   /* host, batch + 1 entries                                 */
+  SwaPackedTensor q, k, v, o, dout;
+  const float* lse;            /* from swa_varlen_fwd                                     */
+  SwaPackedTensor dq, dk, dv;  /* outputs                                                 */
+  const float* sink_logits;    /* optional, as given to the forward                       */
+  float* dsink_logits;         /* [Hq] output when sink_logits is set (else ignored)      */
+  void* workspace;             /* >= swa_varlen_bwd_workspace_size bytes, 256-B aligned   */
+  size_t workspace_bytes;
+} SwaVarlenBwdArgs;
+
+/* Size of the varlen lse buffer in floats (0 for invalid arguments). */
+SWA_API size_t swa_varlen_lse_floats(const SwaProblem* p, const int32_t* cu_seqlens);
+
+/* Scratch swa_varlen_bwd needs: the largest one-sequence swa_bwd_workspace_size. */
+SWA_API size_t swa_varlen_bwd_workspace_size(const SwaProblem* p, const int32_t* cu_seqlens);
+
+/* Forward over packed sequences (swa_fwd per sequence). */
+SWA_API int swa_varlen_fwd(const SwaVarlenFwdArgs* args, void* stream);
+
+/* Backward over packed sequences (swa_bwd per sequence, deterministic; with sink_logits,
+ * dsink_logits sums the sequences' contributions in sequence order). */
+SWA_API int swa_varlen_bwd(const SwaVarlenBwdArgs* args, void* stream);
+
 /* Backward that allocates nothing and takes no workspace.  No counterpart in the reference.
  *
  * For callers that cannot call cudaMalloc: a host that hands this library only its tensors

@@ -146,3 +146,39 @@ def test_dkdv_launch_count():
     assert count(n_q_heads=8, n_kv_heads=8, seq_len=256, head_dim=64, window_size=512, sink_size=4) == 2
     assert count(head_dim=24) == 0
     assert lib.swa_bwd_dkdv_launch_count(None) == 0
+
+
+def test_varlen_sizes_and_argument_errors():
+    # host-only entry points: lse blocks per sequence, the largest one-sequence workspace
+    import numpy as np
+    L = submodule("_lib")
+    lib = pkg().lib()
+    prob = _problem(batch=4, seq_len=0)
+    cu = np.array([0, 100, 100, 229, 1029], dtype=np.int32)
+    floats = lib.swa_varlen_lse_floats(ctypes.byref(prob), cu.ctypes.data)
+    assert floats == 4 * (128 + 0 + 192 + 832)
+    ws = lib.swa_varlen_bwd_workspace_size(ctypes.byref(prob), cu.ctypes.data)
+    one = _problem(batch=1, seq_len=800)
+    assert ws == lib.swa_bwd_workspace_size(ctypes.byref(one))
+    bad = np.array([0, 100, 50, 60, 70], dtype=np.int32)   # decreasing offsets
+    assert lib.swa_varlen_lse_floats(ctypes.byref(prob), bad.ctypes.data) == 0
+    args = L.SwaVarlenFwdArgs(prob, bad.ctypes.data)
+    assert lib.swa_varlen_fwd(ctypes.byref(args), None) == L.SWA_ERR_INVALID_ARG
+    args = L.SwaVarlenFwdArgs(prob, None)
+    assert lib.swa_varlen_fwd(ctypes.byref(args), None) == L.SWA_ERR_INVALID_ARG
+    # no tokens at all: nothing to do, no pointer needed
+    empty = np.zeros(5, dtype=np.int32)
+    args = L.SwaVarlenFwdArgs(prob, empty.ctypes.data)
+    assert lib.swa_varlen_fwd(ctypes.byref(args), None) == L.SWA_OK
+    bargs = L.SwaVarlenBwdArgs(prob, empty.ctypes.data)
+    assert lib.swa_varlen_bwd(ctypes.byref(bargs), None) == L.SWA_OK
+
+
+def test_varlen_cu_seqlens_validation():
+    import numpy as np
+    V = submodule("varlen")
+    assert V._host_cu([0, 3, 3, 10], 10).dtype == np.int32
+    assert list(V._host_cu(torch.tensor([0, 5]), 5)) == [0, 5]
+    for cu, total in (([1, 5], 5), ([0, 5, 4], 5), ([0, 5], 6), ([[0, 5]], 5)):
+        with pytest.raises(ValueError):
+            V._host_cu(cu, total)
