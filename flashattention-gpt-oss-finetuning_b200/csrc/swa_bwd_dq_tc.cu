@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
       bool ok = true;
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
         int b, h, qt;
-        decode_item(it, Hq, n_qt, &b, &h, &qt);
+        decode_item(it, Hq, p.B, n_qt, &b, &h, &qt);
         const int q0 = qt * C::BM;
         const FwdSched sc = fwd_schedule(q0, L, W, S, p.sink_box);
         const int n = sc.n();
@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
       bool ok = true;
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
         int b, h, qt;
-        decode_item(it, Hq, n_qt, &b, &h, &qt);
+        decode_item(it, Hq, p.B, n_qt, &b, &h, &qt);
         const FwdSched sc = fwd_schedule(qt * C::BM, L, W, S, p.sink_box);
         const int n = sc.n();
         if (n == 0) continue;
@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
       bool ok = true;
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
         int b, h, qt;
-        decode_item(it, Hq, n_qt, &b, &h, &qt);
+        decode_item(it, Hq, p.B, n_qt, &b, &h, &qt);
         const FwdSched sc = fwd_schedule(qt * C::BM, L, W, S, p.sink_box);
         const int n = sc.n();
         if (n == 0) continue;
@@ -284,7 +284,7 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
     auto delta_next = [&]() -> bool {
       for (; it_d < n_items; it_d += gridDim.x) {
         int b, h, qt;
-        decode_item(it_d, Hq, n_qt, &b, &h, &qt);
+        decode_item(it_d, Hq, p.B, n_qt, &b, &h, &qt);
         if (fwd_schedule(qt * C::BM, L, W, S, p.sink_box).n() == 0) continue;
         const int qb = dqi % C::NQB;
         if (ok) ok = mbar_wait(&bar_q_full[qb], (dqi / C::NQB) & 1, &abort_sh);
@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
     delta_next();
     for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
       int b, h, qt;
-      decode_item(it, Hq, n_qt, &b, &h, &qt);
+      decode_item(it, Hq, p.B, n_qt, &b, &h, &qt);
       const int i = qt * C::BM + r;
       const int n = fwd_schedule(qt * C::BM, L, W, S, p.sink_box).n();
       const bool have = n > 0;
@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
     bool ok = !dead;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
       int b, h, qt;
-      decode_item(it, Hq, n_qt, &b, &h, &qt);
+      decode_item(it, Hq, p.B, n_qt, &b, &h, &qt);
       const int q0 = qt * C::BM;
       const int i = q0 + r;
       const int rw0 = q0 + quad * 32;  // this warp's 32 rows

@@ -96,10 +96,13 @@ __device__ __forceinline__ DkdvItem dkdv_item(int idx, const BwdParams& p, int G
     const int end = min(total, it.it0 + p.ch);
     it.n = end > it.it0 ? end - it.it0 : 0;
   } else {
+    // (batch, KV head) fastest, key tile slowest from tile 0 up: under a causal mask the
+    // first key tiles have the most queries, so the largest items are taken first
     int r = idx - n_far;
     it.chunk = -1;
-    it.kt = r % n_kt;
-    r /= n_kt;
+    const int units = p.B * p.Hkv;
+    it.kt = r / units;
+    r %= units;
     it.kvh = r % p.Hkv;
     it.b = r / p.Hkv;
     const int first = it.kt * 2;

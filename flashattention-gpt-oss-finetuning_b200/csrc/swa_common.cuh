@@ -237,12 +237,15 @@ __device__ __forceinline__ FwdSched fwd_schedule(int q0, int L, int W, int S, in
 
 // Work item = one 128-row query tile of one (batch, query head).  Items are numbered with the
 // query head fastest, so CTAs running at the same time read the same K/V rows (one GQA group)
-// and share them through L2.
-__device__ __forceinline__ void decode_item(int it, int Hq, int n_qt, int* b, int* h, int* qt) {
+// and share them through L2; then the batch; the query tile is slowest and runs from the last
+// tile down, so under a causal mask the largest items (most keys) are taken first and the
+// persistent CTAs' last items are the short ones (longest-first ordering).
+__device__ __forceinline__ void decode_item(int it, int Hq, int B, int n_qt, int* b, int* h,
+                                            int* qt) {
   *h = it % Hq;
   const int rest = it / Hq;
-  *qt = rest % n_qt;
-  *b = rest / n_qt;
+  *b = rest % B;
+  *qt = n_qt - 1 - rest / B;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -314,6 +317,18 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // 2^x on the special-function unit (ex2.approx, flushes denormal results to zero).
+// Three-input max / min (one sm_100 instruction each; NaN handling as max.f32 / min.f32).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+  float r;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));

@@ -74,46 +74,62 @@ __device__ __forceinline__ float mask_and_max(float* s, bool full, int c_lo, int
       for (int c = 0; c < N; ++c) s[c] = (c <= c_hi && (c >= c_lo || c < c_sk)) ? s[c] : NEG;
     }
   }
-  constexpr int K = N < 8 ? N : 8;
-  float e[K];
+  float r;
+  if constexpr (N >= 16) {
+    // 8 independent chains of three-input max (min) over the N columns, then one tree
+    float e[8];
 #pragma unroll
-  for (int k = 0; k < K; ++k) e[k] = s[k];
-  if (pos) {
+    for (int k = 0; k < 8; ++k) e[k] = s[k];
+    if (pos) {
 #pragma unroll
-    for (int c = K; c < N; ++c) e[c % K] = fmaxf(e[c % K], s[c]);
+      for (int c = 8; c + 16 <= N; c += 16)
 #pragma unroll
-    for (int k = K / 2; k > 0; k >>= 1)
+        for (int k = 0; k < 8; ++k) e[k] = max3f(e[k], s[c + k], s[c + 8 + k]);
+      if constexpr ((N - 8) % 16 != 0) {
 #pragma unroll
-      for (int j = 0; j < k; ++j) e[j] = fmaxf(e[j], e[j + k]);
+        for (int k = 0; k < 8; ++k) e[k] = fmaxf(e[k], s[N - 8 + k]);
+      }
+      r = max3f(max3f(e[0], e[1], e[2]), max3f(e[3], e[4], e[5]), fmaxf(e[6], e[7]));
+    } else {
+#pragma unroll
+      for (int c = 8; c + 16 <= N; c += 16)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) e[k] = min3f(e[k], s[c + k], s[c + 8 + k]);
+      if constexpr ((N - 8) % 16 != 0) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) e[k] = fminf(e[k], s[N - 8 + k]);
+      }
+      r = min3f(min3f(e[0], e[1], e[2]), min3f(e[3], e[4], e[5]), fminf(e[6], e[7]));
+    }
   } else {
+    r = s[0];
 #pragma unroll
-    for (int c = K; c < N; ++c) e[c % K] = fminf(e[c % K], s[c]);
-#pragma unroll
-    for (int k = K / 2; k > 0; k >>= 1)
-#pragma unroll
-      for (int j = 0; j < k; ++j) e[j] = fminf(e[j], e[j + k]);
+    for (int c = 1; c < N; ++c) r = pos ? fmaxf(r, s[c]) : fminf(r, s[c]);
   }
-  return (e[0] == NEG) ? -INFINITY : e[0] * sl2;
+  return (r == NEG) ? -INFINITY : r * sl2;
 }
 
 // P = 2^(s * scale - base) for N columns, packed to 16-bit pairs and stored to TMEM (N/2
 // columns at tP_lane); returns the row sum of P (fp32).
 template <typename T, int N>
 __device__ __forceinline__ float exp_pack_store(const float* s, float sl2, float base, uint32_t tP_lane) {
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  // two columns per instruction on the packed fp32 pipe (same roundings as scalar fmaf/add)
+  const float2 sl2v = make_float2(sl2, sl2), nb = make_float2(-base, -base);
+  float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
   for (int g = 0; g < N / 16; ++g) {
     uint32_t pw[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const float p0 = fast_exp2(fmaf(s[g * 16 + 2 * e], sl2, -base));
-      const float p1 = fast_exp2(fmaf(s[g * 16 + 2 * e + 1], sl2, -base));
-      acc[e & 3] += p0 + p1;
-      pw[e] = Pack<T>::pack(p0, p1);
+      const float2 t = __ffma2_rn(make_float2(s[g * 16 + 2 * e], s[g * 16 + 2 * e + 1]), sl2v, nb);
+      const float2 pr = make_float2(fast_exp2(t.x), fast_exp2(t.y));
+      acc[e & 1] = __fadd2_rn(acc[e & 1], pr);
+      pw[e] = Pack<T>::pack(pr.x, pr.y);
     }
     tmem_st8(tP_lane + g * 8, pw);
   }
-  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  const float2 a = __fadd2_rn(acc[0], acc[1]);
+  return a.x + a.y;
 }
 
 template <int N>
@@ -220,7 +236,7 @@ __global__ void __launch_bounds__(224, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
       bool ok = true;
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
         int b, h, qt;
-        decode_item(it, Hq, n_qt, &b, &h, &qt);
+        decode_item(it, Hq, p.B, n_qt, &b, &h, &qt);
         const int q0 = qt * C::BM;
         const FwdSched sc = fwd_schedule(q0, L, W, S, p.sink_box);
         const int n = sc.n();
@@ -263,7 +279,7 @@ __global__ void __launch_bounds__(224, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
       bool ok = true;
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
         int b, h, qt;
-        decode_item(it, Hq, n_qt, &b, &h, &qt);
+        decode_item(it, Hq, p.B, n_qt, &b, &h, &qt);
         const FwdSched sc = fwd_schedule(qt * C::BM, L, W, S, p.sink_box);
         const int n = sc.n();
         if (n == 0) continue;
@@ -305,7 +321,7 @@ __global__ void __launch_bounds__(224, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
       bool ok = true;
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
         int b, h, qt;
-        decode_item(it, Hq, n_qt, &b, &h, &qt);
+        decode_item(it, Hq, p.B, n_qt, &b, &h, &qt);
         const FwdSched sc = fwd_schedule(qt * C::BM, L, W, S, p.sink_box);
         const int n = sc.n();
         if (n == 0) continue;
@@ -345,7 +361,7 @@ __global__ void __launch_bounds__(224, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
     bool ok = true;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
       int b, h, qt;
-      decode_item(it, Hq, n_qt, &b, &h, &qt);
+      decode_item(it, Hq, p.B, n_qt, &b, &h, &qt);
       const int q0 = qt * C::BM;
       const int i = q0 + r;
       const int r0w = q0 + quad * 32;  // this warp's 32 rows
