@@ -12,6 +12,9 @@ max-over-ranks device time are the only cross-rank traffic.
                    (global batch = N x B);
   --scaling strong the workload is fixed and its units are split over the ranks (e.g.
                    cfg4_long_swa: 8 KV heads over 1/2/4/8 GPUs).
+  --scaling seq    the workload is fixed and its sequence is split over the ranks
+                   (seqsplit.py: K/V halo and sink rows exchanged over NCCL inside the timed
+                   step, halo dK/dV and sink partials sent back).
 
 Prints ONE JSON line (rank 0).
 """
@@ -35,6 +38,7 @@ PKG = importlib.import_module("flashattention-gpt-oss-finetuning_b200")
 wl = importlib.import_module("flashattention-gpt-oss-finetuning_b200.workloads")
 plan_mod = importlib.import_module("flashattention-gpt-oss-finetuning_b200.plan")
 sh_mod = importlib.import_module("flashattention-gpt-oss-finetuning_b200.sharding")
+seq_mod = importlib.import_module("flashattention-gpt-oss-finetuning_b200.seqsplit")
 
 METRIC = "fwd+bwd effective TFLOP/s (window+sink FLOPs only)"
 UNIT = "TFLOP/s"
@@ -376,6 +380,54 @@ def run_ours(args, w_job, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_seq(args, w, rank, world, local_rank):
+    """Sequence split: rank r holds rows split_bounds(L, world)[r] of the whole workload."""
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    a, b = seq_mod.split_bounds(w.seq_len, world)[rank]
+    q, k, v, do = (t[:, :, a:b].contiguous().to(dev) for t in wl.make_inputs(w))
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        o, st = seq_mod.seq_sharded_forward(q, k, v, w.seq_len, w.window_size, w.sink_size)
+        return seq_mod.seq_sharded_backward(st, do)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local_rank) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    clk = clocks.stop() if clocks else None
+    ms = max_over_ranks(e0.elapsed_time(e1), dev) / args.steps
+    if rank != 0:
+        return
+    value = wl.useful_flops(w) / (ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16" if w.dtype == torch.bfloat16 else "f16",
+        "data": "synthetic (seeded randn of the workload's shape; no dataset)",
+        "config": dict(w.describe(), parallelism=f"seq{world}: sequence split, K/V halo over NCCL",
+                       rows_per_rank=b - a),
+        "clocks": clk, "e2e": None, "roofline": None,
+        "note": "secondary mode; exchanges (sink broadcast, halo send/recv, halo dK/dV return, "
+                "sink reduce) and the local prefix copies are inside the timed step",
+    }
+    print(json.dumps(line), flush=True)
+
+
 # DRAM bytes (read + write) per launch from one ncu capture, keyed by (workload, kernel)
 # (the dK/dV capture of the cfg2 step: 581.4 MB read + 28.8 MB written).
 TRAFFIC: dict = {("cfg2_gptoss_swa", "bwd_dkdv"): 610_271_744}
@@ -388,7 +440,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="cfg2_gptoss_swa", choices=sorted(wl.CONFIGS))
-    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--scaling", choices=["weak", "strong", "seq"], default="weak")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -405,7 +457,10 @@ def main():
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, w, rank, world, local_rank)
+        if args.scaling == "seq":
+            run_seq(args, w, rank, world, local_rank)
+        else:
+            run_ours(args, w, rank, world, local_rank)
     finally:
         if torch.distributed.is_initialized():
             torch.distributed.destroy_process_group()

@@ -82,15 +82,18 @@ def _default_bwd(q, k, v, o, lse, do, w, s, scale):
 
 def _prefixed(x: torch.Tensor, pre: int, head: Optional[torch.Tensor] = None,
               tail: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """[B, H, pre + n, D]: zeros, `head` at rows [0, head_n), `tail` ending at row pre, then x."""
+    """[B, H, pre + n, D]: `head` at rows [0, head_n), zeros, `tail` ending at row pre, then x
+    (one concatenation: x is read once and the result written once)."""
     b, h, n, d = x.shape
-    out = x.new_zeros((b, h, pre + n, d))
-    if head is not None and head.shape[2]:
-        out[:, :, :head.shape[2]] = head
-    if tail is not None and tail.shape[2]:
-        out[:, :, pre - tail.shape[2]:pre] = tail
-    out[:, :, pre:] = x
-    return out
+    hn = head.shape[2] if head is not None else 0
+    tn = tail.shape[2] if tail is not None else 0
+    parts = [head] if hn else []
+    if pre - hn - tn > 0:
+        parts.append(x.new_zeros((b, h, pre - hn - tn, d)))
+    if tn:
+        parts.append(tail)
+    parts.append(x)
+    return torch.cat(parts, dim=2) if len(parts) > 1 else x
 
 
 def _staged(group, device) -> bool:
@@ -144,6 +147,24 @@ def _reduce0(t: torch.Tensor, group):
         dist.reduce(t, dst=_global(group, 0), group=group)
 
 
+_SIDE = {}
+
+
+def _side_stream(device):
+    """One side stream per device for the exchanges (created once)."""
+    if device not in _SIDE:
+        _SIDE[device] = torch.cuda.Stream(device)
+    return _SIDE[device]
+
+
+class _nullctx:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
 class SeqShardState:
     """What the backward needs from the forward of one rank."""
 
@@ -165,17 +186,30 @@ def seq_sharded_forward(q, k, v, seq_len: int, window_size: int, sink_size: int 
         softmax_scale = q.shape[-1] ** -0.5
     s = max(0, min(sink_size, seq_len))
     b, hkv, _, d = k.shape
-    # sink rows from rank 0
-    kvs = torch.cat([k[:, :, :s], v[:, :, :s]], 1).contiguous() if rank == 0 else \
-        k.new_empty((b, 2 * hkv, s, d))
-    if world > 1 and s > 0:
-        _broadcast0(kvs, group)
-    # halo rows from the previous rank: it sends its last W'(rank + 1) rows
-    nxt_halo = layout(seq_len, world, rank + 1, window_size, sink_size)[2] if rank + 1 < world else 0
-    send = torch.cat([k[:, :, k.shape[2] - nxt_halo:], v[:, :, v.shape[2] - nxt_halo:]], 1) \
-        if nxt_halo > 0 else None
-    recv_shape = ((b, 2 * hkv, halo, d), k.dtype, k.device) if halo > 0 else None
-    got = _exchange(send, recv_shape, rank, world, group)
+    # the exchanges run on a side stream, beside the query prefix copy or rank 0's forward
+    main = torch.cuda.current_stream(q.device) if q.is_cuda else None
+    side = _side_stream(q.device) if q.is_cuda else None
+    if side is not None:
+        side.wait_stream(main)
+    with torch.cuda.stream(side) if side is not None else _nullctx():
+        # sink rows from rank 0
+        kvs = torch.cat([k[:, :, :s], v[:, :, :s]], 1).contiguous() if rank == 0 else \
+            k.new_empty((b, 2 * hkv, s, d))
+        if world > 1 and s > 0:
+            _broadcast0(kvs, group)
+        # halo rows from the previous rank: it sends its last W'(rank + 1) rows
+        nxt_halo = layout(seq_len, world, rank + 1, window_size, sink_size)[2] \
+            if rank + 1 < world else 0
+        send = torch.cat([k[:, :, k.shape[2] - nxt_halo:], v[:, :, v.shape[2] - nxt_halo:]], 1) \
+            if nxt_halo > 0 else None
+        recv_shape = ((b, 2 * hkv, halo, d), k.dtype, k.device) if halo > 0 else None
+        got = _exchange(send, recv_shape, rank, world, group)
+    ql = _prefixed(q, pre) if rank > 0 else q
+    if side is not None and rank > 0:   # rank 0's own forward needs nothing it receives
+        main.wait_stream(side)
+        for t in (kvs, got, send):
+            if t is not None:
+                t.record_stream(main)
     if rank == 0:
         o, lse = fwd_fn(q, k, v, window_size, sink_size, softmax_scale)
         return o, SeqShardState(rank=rank, world=world, pre=0, halo=0, s=s, q=q, k=k, v=v, o=o,
@@ -185,7 +219,6 @@ def seq_sharded_forward(q, k, v, seq_len: int, window_size: int, sink_size: int 
     vh = got[:, hkv:] if got is not None else None
     kl = _prefixed(k, pre, kvs[:, :hkv], kh)
     vl = _prefixed(v, pre, kvs[:, hkv:], vh)
-    ql = _prefixed(q, pre)
     ol, lse = fwd_fn(ql, kl, vl, window_size, sink_size, softmax_scale)
     return ol[:, :, pre:], SeqShardState(rank=rank, world=world, pre=pre, halo=halo, s=s, q=ql,
                                          k=kl, v=vl, o=ol, lse=lse, w=window_size,
@@ -199,11 +232,14 @@ def seq_sharded_backward(st: SeqShardState, do, bwd_fn: Callable = _default_bwd)
     dol = do if rank == 0 else _prefixed(do.to(st.q.dtype), pre)
     dql, dkl, dvl = bwd_fn(st.q, st.k, st.v, st.o, st.lse, dol, st.w, st.sink, st.scale)
     n = dql.shape[2] - pre
-    dq = dql[:, :, pre:]
-    acc = torch.promote_types(dkl.dtype, torch.float32)  # sums in fp32 (or wider)
-    dk = dkl[:, :, pre:].to(acc)
-    dv = dvl[:, :, pre:].to(acc)
+    dq, dk, dv = dql[:, :, pre:], dkl[:, :, pre:], dvl[:, :, pre:]
+    acc = torch.promote_types(dkl.dtype, torch.float32)  # the added rows sum in fp32 (or wider)
     hkv = dkl.shape[1]
+
+    def add_rows(rows: slice, extra: torch.Tensor):
+        for t, e in ((dk, extra[:, :hkv]), (dv, extra[:, hkv:])):
+            t[:, :, rows] = (t[:, :, rows].to(acc) + e).to(t.dtype)
+
     # halo gradients go back to the previous rank, which owns those keys
     send = torch.cat([dkl[:, :, pre - st.halo:pre], dvl[:, :, pre - st.halo:pre]], 1).to(acc) \
         if st.halo > 0 else None
@@ -212,17 +248,15 @@ def seq_sharded_backward(st: SeqShardState, do, bwd_fn: Callable = _default_bwd)
         if nxt_halo > 0 else None
     got = _exchange(send, shape, rank, world, group, reverse=True)
     if got is not None:
-        dk[:, :, n - nxt_halo:] += got[:, :hkv]
-        dv[:, :, n - nxt_halo:] += got[:, hkv:]
+        add_rows(slice(n - nxt_halo, n), got)
     # sink rows: every rank's partial summed onto rank 0
     if world > 1 and st.s > 0:
         part = torch.cat([dkl[:, :, :st.s], dvl[:, :, :st.s]], 1).to(acc) if rank > 0 else \
             torch.zeros((dk.shape[0], 2 * hkv, st.s, dk.shape[3]), dtype=acc, device=dk.device)
         _reduce0(part, group)
         if rank == 0:
-            dk[:, :, :st.s] += part[:, :hkv]
-            dv[:, :, :st.s] += part[:, hkv:]
-    return dq, dk.to(dkl.dtype), dv.to(dvl.dtype)
+            add_rows(slice(0, st.s), part)
+    return dq, dk, dv
 
 
 class SeqShardedSWDA(torch.autograd.Function):
