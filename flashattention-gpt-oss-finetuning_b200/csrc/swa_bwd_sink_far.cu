@@ -62,16 +62,27 @@ struct FarUnit {
   int b, kvh, u0, n;  // items [u0, u0 + n) of the group's G * nf
 };
 
+// Units are numbered with the (batch, KV head) fastest and the chunk slowest, and a chunk's
+// items run tile-major from the last far tile down (all G query heads of a tile together): the
+// dK/dV pass launched just before ends on the last key tiles, so the Q / dO rows read first
+// here are the ones it left in L2.
 __device__ __forceinline__ FarUnit far_unit(int idx, const BwdParams& p, int G) {
   FarUnit f;
-  const int c = idx % p.fk_u;
-  const int r = idx / p.fk_u;
+  const int units = p.B * p.Hkv;
+  const int c = idx / units;
+  const int r = idx % units;
   f.kvh = r % p.Hkv;
   f.b = r / p.Hkv;
   f.u0 = c * p.fk_c;
   const int total = G * p.nf;
   f.n = min(p.fk_c, total - f.u0);
   return f;
+}
+
+// Item u of a (batch, KV head): query head kvh * G + *hg and far 128-row tile *tile.
+__device__ __forceinline__ void far_item(int u, const BwdParams& p, int G, int* hg, int* tile) {
+  *hg = u % G;
+  *tile = p.nf - 1 - u / G;
 }
 
 template <typename T, int D>
@@ -139,9 +150,10 @@ __global__ void __launch_bounds__(192, 1) bwd_sink_far_kernel(const __grid_const
         for (int t = 0; t < fu.n; ++t, ++gi) {
           const int st = gi % C::NSTG;
           if (gi >= C::NSTG && !(ok = mbar_wait(&bar_empty[st], ((gi / C::NSTG) - 1) & 1, &abort_sh))) break;
-          const int u = fu.u0 + t;
-          const int h = fu.kvh * G + u / p.nf;
-          const int q0 = (p.qf0 + u % p.nf) * C::BM;
+          int hg, tile;
+          far_item(fu.u0 + t, p, G, &hg, &tile);
+          const int h = fu.kvh * G + hg;
+          const int q0 = (p.qf0 + tile) * C::BM;
           const int row = fu.b * p.Hq + h;
           unsigned char* Sb = STs + st * C::STAGE;
           mbar_arrive_expect_tx(&bar_full[st], 2 * C::QT_BYTES + 1024);
@@ -232,8 +244,9 @@ __global__ void __launch_bounds__(192, 1) bwd_sink_far_kernel(const __grid_const
         const int st = gi % C::NSTG;
         if (!(ok = mbar_wait(&bar_s, gi & 1, &abort_sh))) break;
         tc_fence_after();
-        const int u = fu.u0 + t;
-        const int i = (p.qf0 + u % p.nf) * C::BM + r;
+        int hg, tile;
+        far_item(fu.u0 + t, p, G, &hg, &tile);
+        const int i = (p.qf0 + tile) * C::BM + r;
         const bool on = i >= p.rfar && i < p.L;
         unsigned char* Sb = STs + st * C::STAGE;
         const float lse_r = reinterpret_cast<const float*>(Sb + 2 * C::QT_BYTES)[r];
