@@ -428,6 +428,96 @@ def run_seq(args, w, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_variant(args, w, local_rank):
+    """1-GPU lines for the additional modes (not the headline): learned sink logits on the
+    workload's shape, or a packed variable-length batch of the workload's head layout."""
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    F = PKG.flash_attention_gpt_oss
+    V = importlib.import_module("flashattention-gpt-oss-finetuning_b200.varlen")
+    stream = torch.cuda.current_stream(dev)
+    extra = {}
+    if args.variant == "sink_logits":
+        q, k, v, do = wl.make_inputs(w, device=dev)
+        g = torch.Generator().manual_seed(w.seed)
+        sl = (torch.randn(w.n_q_heads, generator=g) * 2).to(dev)
+        flops = wl.useful_flops(w)
+
+        def step():
+            o, lse = F.swa_forward(q, k, v, w.window_size, w.sink_size, sink_logits=sl)
+            F.swa_backward(q, k, v, o, lse, do, w.window_size, w.sink_size, sink_logits=sl)
+        cfg = dict(w.describe(), variant="learned per-head sink logits + token sinks")
+    else:
+        g = torch.Generator().manual_seed(w.seed)
+        n_seq = 32
+        lens = torch.randint(128, w.seq_len // 2 + 1, (n_seq,), generator=g).tolist()
+        cu = [0]
+        for n in lens:
+            cu.append(cu[-1] + n)
+        t = cu[-1]
+        q, do = ((torch.randn(t, w.n_q_heads, w.head_dim, generator=g) * w.input_scale)
+                 .to(w.dtype).to(dev) for _ in range(2))
+        k, v = ((torch.randn(t, w.n_kv_heads, w.head_dim, generator=g) * w.input_scale)
+                .to(w.dtype).to(dev) for _ in range(2))
+        flops = sum(wl.useful_flops(w.replace(batch=1, seq_len=n)) for n in lens)
+
+        def step():
+            o, lse, cuh = V.swa_varlen_forward(q, k, v, cu, w.window_size, w.sink_size)
+            V.swa_varlen_backward(q, k, v, o, lse, cuh, do, w.window_size, w.sink_size)
+        # the same sequences padded to a dense batch, as without the packed mode
+        lmax = max(lens)
+        qd = torch.zeros(n_seq, w.n_q_heads, lmax, w.head_dim, dtype=w.dtype, device=dev)
+        kd = torch.zeros(n_seq, w.n_kv_heads, lmax, w.head_dim, dtype=w.dtype, device=dev)
+        vd, dod = torch.zeros_like(kd), torch.zeros_like(qd)
+        for i, n in enumerate(lens):
+            a = cu[i]
+            qd[i, :, :n] = q[a:a + n].transpose(0, 1)
+            kd[i, :, :n] = k[a:a + n].transpose(0, 1)
+            vd[i, :, :n] = v[a:a + n].transpose(0, 1)
+            dod[i, :, :n] = do[a:a + n].transpose(0, 1)
+
+        def dense_step():
+            o, lse = F.swa_forward(qd, kd, vd, w.window_size, w.sink_size)
+            F.swa_backward(qd, kd, vd, o, lse, dod, w.window_size, w.sink_size)
+        for _ in range(args.warmup):
+            dense_step()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            dense_step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        dms = e0.elapsed_time(e1) / args.steps
+        extra["padded_dense"] = {"ms_per_step": dms, "value": flops / (dms * 1e-3) / 1e12,
+                                 "note": "same sequences zero-padded to [32, H, max_len, D]"}
+        cfg = dict(w.describe(), variant="packed variable-length batch", n_seq=n_seq,
+                   total_tokens=t, min_len=min(lens), max_len=lmax)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    line = {
+        "metric": METRIC, "value": flops / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16" if w.dtype == torch.bfloat16 else "f16",
+        "data": "synthetic (seeded randn; no dataset)", "config": cfg, "clocks": clk,
+        "e2e": None, "roofline": None, **extra,
+        "note": "additional mode (not the headline); Python API with inputs resident on the GPU",
+    }
+    print(json.dumps(line), flush=True)
+
+
 # DRAM bytes (read + write) per launch from one ncu capture, keyed by (workload, kernel)
 # (the dK/dV capture of the cfg2 step: 581.4 MB read + 28.8 MB written).
 TRAFFIC: dict = {("cfg2_gptoss_swa", "bwd_dkdv"): 610_271_744}
@@ -441,6 +531,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="cfg2_gptoss_swa", choices=sorted(wl.CONFIGS))
     ap.add_argument("--scaling", choices=["weak", "strong", "seq"], default="weak")
+    ap.add_argument("--variant", choices=["plain", "sink_logits", "varlen"], default="plain",
+                    help="additional modes, 1 GPU (default: the headline path)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -457,7 +549,9 @@ def main():
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     try:
-        if args.scaling == "seq":
+        if args.variant != "plain":
+            run_variant(args, w, local_rank)
+        elif args.scaling == "seq":
             run_seq(args, w, rank, world, local_rank)
         else:
             run_ours(args, w, rank, world, local_rank)

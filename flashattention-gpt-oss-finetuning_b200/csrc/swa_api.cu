@@ -353,6 +353,71 @@ bool packed_ok(const SwaPackedTensor& t) {
   return t.ptr && t.stride_t >= 0 && t.stride_h >= 0 && t.stride_t % 8 == 0 && t.stride_h % 8 == 0;
 }
 
+// Sequences run on a small per-device pool of streams, forked from and joined back into the
+// caller's stream with events, so that short sequences (whose launches alone would leave most
+// SMs idle) overlap.  Every sequence writes disjoint outputs and owns its workspace region, so
+// the overlap changes no result.
+constexpr int kVarlenStreams = 4;
+std::mutex g_pool_mu;
+cudaStream_t g_pool[kMaxDev][kVarlenStreams] = {};
+
+int varlen_streams(cudaStream_t** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return record(e);
+  if (dev < 0 || dev >= kMaxDev) return SWA_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_pool_mu);
+  for (int i = 0; i < kVarlenStreams; ++i)
+    if (!g_pool[dev][i] &&
+        (e = cudaStreamCreateWithFlags(&g_pool[dev][i], cudaStreamNonBlocking)) != cudaSuccess)
+      return record(e);
+  *out = g_pool[dev];
+  return SWA_OK;
+}
+
+// Fork `n` pool streams from `s` (n = 0: run everything on `s`).
+struct Fork {
+  cudaStream_t base;
+  cudaStream_t* pool = nullptr;
+  int n = 0;
+  int begin(cudaStream_t s, int n_seq) {
+    base = s;
+    if (n_seq < 2) return SWA_OK;
+    int st = varlen_streams(&pool);
+    if (st) return st;
+    n = n_seq < kVarlenStreams ? n_seq : kVarlenStreams;
+    cudaEvent_t ev;
+    cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(ev, s);
+    for (int i = 0; i < n && e == cudaSuccess; ++i) e = cudaStreamWaitEvent(pool[i], ev, 0);
+    cudaEventDestroy(ev);
+    if (e != cudaSuccess) n = 0;
+    return record(e);
+  }
+  cudaStream_t stream(int i) const { return n ? pool[i % n] : base; }
+  // Join every forked stream back into the base stream (also after an error).
+  int end() {
+    cudaError_t first = cudaSuccess;
+    for (int i = 0; i < n; ++i) {
+      cudaEvent_t ev;
+      cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+      if (e == cudaSuccess) {
+        e = cudaEventRecord(ev, pool[i]);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(base, ev, 0);
+        cudaEventDestroy(ev);
+      }
+      if (first == cudaSuccess) first = e;
+    }
+    n = 0;
+    return record(first);
+  }
+};
+
+size_t seq_ws_bytes(const SwaProblem& p, int L) {
+  const SwaProblem q = seq_problem(p, L);
+  return (swa_bwd_workspace_size(&q) + 255) & ~(size_t)255;
+}
+
 }  // namespace
 
 extern "C" {
@@ -366,13 +431,10 @@ size_t swa_varlen_lse_floats(const SwaProblem* p, const int32_t* cu) {
 
 size_t swa_varlen_bwd_workspace_size(const SwaProblem* p, const int32_t* cu) {
   if (check_cu(p, cu) != SWA_OK) return 0;
-  size_t m = 0;
-  for (int b = 0; b < p->batch; ++b) {
-    const SwaProblem q = seq_problem(*p, cu[b + 1] - cu[b]);
-    const size_t w = swa_bwd_workspace_size(&q);
-    m = w > m ? w : m;
-  }
-  return m;
+  size_t n = 0;
+  for (int b = 0; b < p->batch; ++b)
+    if (cu[b + 1] > cu[b]) n += seq_ws_bytes(*p, cu[b + 1] - cu[b]);
+  return n;
 }
 
 int swa_varlen_fwd(const SwaVarlenFwdArgs* a, void* stream) {
@@ -386,8 +448,12 @@ int swa_varlen_fwd(const SwaVarlenFwdArgs* a, void* stream) {
   for (const SwaPackedTensor* t : need)
     if (!packed_ok(*t)) return SWA_ERR_INVALID_ARG;
   if (!a->lse) return SWA_ERR_INVALID_ARG;
+  int n_seq = 0;
+  for (int b = 0; b < a->p.batch; ++b) n_seq += cu[b + 1] > cu[b];
+  Fork fk;
+  if ((st = fk.begin(static_cast<cudaStream_t>(stream), n_seq))) return st;
   size_t lse_off = 0;
-  for (int b = 0; b < a->p.batch; ++b) {
+  for (int b = 0, i = 0; b < a->p.batch && !st; ++b) {
     const int L = cu[b + 1] - cu[b];
     if (L == 0) continue;
     SwaFwdArgs f;
@@ -395,10 +461,11 @@ int swa_varlen_fwd(const SwaVarlenFwdArgs* a, void* stream) {
     f.q = seq_view(a->q, cu[b]); f.k = seq_view(a->k, cu[b]);
     f.v = seq_view(a->v, cu[b]); f.o = seq_view(a->o, cu[b]);
     f.lse = a->lse + lse_off;
-    if ((st = fwd_impl(&f, a->sink_logits, stream))) return st;
+    st = fwd_impl(&f, a->sink_logits, fk.stream(i++));
     lse_off += (size_t)a->p.n_q_heads * swa::stat_row_stride(L);
   }
-  return SWA_OK;
+  const int je = fk.end();
+  return st ? st : je;
 }
 
 int swa_varlen_bwd(const SwaVarlenBwdArgs* a, void* stream) {
@@ -409,42 +476,59 @@ int swa_varlen_bwd(const SwaVarlenBwdArgs* a, void* stream) {
   if (a->sink_logits && !a->dsink_logits) return SWA_ERR_INVALID_ARG;
   const int32_t* cu = a->cu_seqlens;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  bool wrote_dsinks = false;
-  if (cu[a->p.batch] > 0) {
-    const SwaPackedTensor* need[] = {&a->q, &a->k, &a->v, &a->o, &a->dout, &a->dq, &a->dk, &a->dv};
-    for (const SwaPackedTensor* t : need)
-      if (!packed_ok(*t)) return SWA_ERR_INVALID_ARG;
-    if (!a->lse) return SWA_ERR_INVALID_ARG;
-    if (a->workspace_bytes < swa_varlen_bwd_workspace_size(&a->p, cu)) return SWA_ERR_WORKSPACE;
-    size_t lse_off = 0;
-    for (int b = 0; b < a->p.batch; ++b) {
-      const int L = cu[b + 1] - cu[b];
-      if (L == 0) continue;
-      SwaBwdArgs g;
-      g.p = seq_problem(a->p, L);
-      g.q = seq_view(a->q, cu[b]); g.k = seq_view(a->k, cu[b]); g.v = seq_view(a->v, cu[b]);
-      g.o = seq_view(a->o, cu[b]); g.dout = seq_view(a->dout, cu[b]);
-      g.dq = seq_view(a->dq, cu[b]); g.dk = seq_view(a->dk, cu[b]); g.dv = seq_view(a->dv, cu[b]);
-      g.lse = a->lse + lse_off;
-      g.workspace = a->workspace;           // reused in stream order, one sequence at a time
-      g.workspace_bytes = a->workspace_bytes;
-      swa::BwdParams kp;
-      if ((st = build_bwd(&g, &kp))) return st;
-      if ((st = dispatch<Dq>(g.p, kp, s))) return st;
-      if ((st = dispatch<Dkdv>(g.p, kp, s))) return st;
-      if (a->sink_logits) {
-        if ((st = record(swa::launch_sink_logit_grad(g.lse, kp.delta, a->sink_logits,
-                                                     a->dsink_logits, 1, a->p.n_q_heads,
-                                                     kp.lse_ld, wrote_dsinks, s))))
-          return st;
-        wrote_dsinks = true;
-      }
-      lse_off += (size_t)a->p.n_q_heads * swa::stat_row_stride(L);
-    }
-  }
-  if (a->sink_logits && !wrote_dsinks)  // no tokens at all: d sink = 0
+  if (cu[a->p.batch] == 0) {
+    if (!a->sink_logits) return SWA_OK;  // no tokens at all: d sink = 0
     return record(swa::launch_sink_logit_grad(nullptr, nullptr, a->sink_logits, a->dsink_logits,
                                               0, a->p.n_q_heads, 0, false, s));
+  }
+  const SwaPackedTensor* need[] = {&a->q, &a->k, &a->v, &a->o, &a->dout, &a->dq, &a->dk, &a->dv};
+  for (const SwaPackedTensor* t : need)
+    if (!packed_ok(*t)) return SWA_ERR_INVALID_ARG;
+  if (!a->lse) return SWA_ERR_INVALID_ARG;
+  if (!a->workspace || a->workspace_bytes < swa_varlen_bwd_workspace_size(&a->p, cu))
+    return SWA_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(a->workspace) & 255u) return SWA_ERR_WORKSPACE;
+  int n_seq = 0;
+  for (int b = 0; b < a->p.batch; ++b) n_seq += cu[b + 1] > cu[b];
+  Fork fk;
+  if ((st = fk.begin(s, n_seq))) return st;
+  size_t lse_off = 0, ws_off = 0;
+  for (int b = 0, i = 0; b < a->p.batch && !st; ++b) {
+    const int L = cu[b + 1] - cu[b];
+    if (L == 0) continue;
+    SwaBwdArgs g;
+    g.p = seq_problem(a->p, L);
+    g.q = seq_view(a->q, cu[b]); g.k = seq_view(a->k, cu[b]); g.v = seq_view(a->v, cu[b]);
+    g.o = seq_view(a->o, cu[b]); g.dout = seq_view(a->dout, cu[b]);
+    g.dq = seq_view(a->dq, cu[b]); g.dk = seq_view(a->dk, cu[b]); g.dv = seq_view(a->dv, cu[b]);
+    g.lse = a->lse + lse_off;
+    g.workspace = static_cast<char*>(a->workspace) + ws_off;  // this sequence's own region
+    g.workspace_bytes = seq_ws_bytes(a->p, L);
+    swa::BwdParams kp;
+    const cudaStream_t si = fk.stream(i++);
+    if (!(st = build_bwd(&g, &kp)) && !(st = dispatch<Dq>(g.p, kp, si)))
+      st = dispatch<Dkdv>(g.p, kp, si);
+    lse_off += (size_t)a->p.n_q_heads * swa::stat_row_stride(L);
+    ws_off += g.workspace_bytes;
+  }
+  const int je = fk.end();
+  if (st || je) return st ? st : je;
+  if (!a->sink_logits) return SWA_OK;
+  // d sink: the sequences' sums added in sequence order on the caller's stream (deterministic)
+  lse_off = ws_off = 0;
+  bool wrote = false;
+  for (int b = 0; b < a->p.batch; ++b) {
+    const int L = cu[b + 1] - cu[b];
+    if (L == 0) continue;
+    const float* delta = reinterpret_cast<const float*>(static_cast<const char*>(a->workspace) + ws_off);
+    if ((st = record(swa::launch_sink_logit_grad(a->lse + lse_off, delta, a->sink_logits,
+                                                 a->dsink_logits, 1, a->p.n_q_heads,
+                                                 swa::stat_row_stride(L), wrote, s))))
+      return st;
+    wrote = true;
+    lse_off += (size_t)a->p.n_q_heads * swa::stat_row_stride(L);
+    ws_off += seq_ws_bytes(a->p, L);
+  }
   return SWA_OK;
 }
 

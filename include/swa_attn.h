@@ -149,7 +149,9 @@ SWA_API int swa_bwd_sink_logits(const SwaBwdArgs* args, const float* sink_logits
  * non-decreasing int32 offsets starting at 0.  SwaProblem.seq_len is ignored.
  * lse: n_q_heads * swa_varlen_lse_floats(...) fp32; sequence b owns a [Hq, round_up(L_b, 64)]
  * block after those of sequences 0..b-1.  Every sequence runs the dense kernels as a
- * one-sequence problem on `stream`, in order.
+ * one-sequence problem; the sequences are spread over a pool of 4 library-owned streams per
+ * device (created on first use, kept until exit) that fork from and join back into `stream`
+ * with events, so they overlap on the GPU while the call stays ordered on `stream`.
  * ------------------------------------------------------------------------------------ */
 
 /* A packed [T, H, D] tensor: device pointer + element strides of the token and head dims. */
@@ -182,7 +184,8 @@ typedef struct SwaVarlenBwdArgs {
 /* Size of the varlen lse buffer in floats (0 for invalid arguments). */
 SWA_API size_t swa_varlen_lse_floats(const SwaProblem* p, const int32_t* cu_seqlens);
 
-/* Scratch swa_varlen_bwd needs: the largest one-sequence swa_bwd_workspace_size. */
+/* Scratch swa_varlen_bwd needs: one 256-byte aligned swa_bwd_workspace_size region per
+ * non-empty sequence (sequences overlap on the GPU, each with its own region). */
 SWA_API size_t swa_varlen_bwd_workspace_size(const SwaProblem* p, const int32_t* cu_seqlens);
 
 /* Forward over packed sequences (swa_fwd per sequence). */
