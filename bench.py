@@ -518,9 +518,10 @@ def run_variant(args, w, local_rank):
     print(json.dumps(line), flush=True)
 
 
-# DRAM bytes (read + write) per launch from one ncu capture, keyed by (workload, kernel)
-# (the dK/dV capture of the cfg2 step: 581.4 MB read + 28.8 MB written).
-TRAFFIC: dict = {("cfg2_gptoss_swa", "bwd_dkdv"): 610_271_744}
+# DRAM bytes (read + write) per step of a phase from one ncu capture, keyed by (workload,
+# phase): the dK/dV phase of cfg2 = dK/dV kernel 345.6 MB + far sink-pair kernel 261.0 MB
+# (profiles/step_cfg2_dram_traffic.md).
+TRAFFIC: dict = {("cfg2_gptoss_swa", "bwd_dkdv"): 322_498_560 + 23_117_824 + 259_731_712 + 1_313_792}
 
 
 def main():
