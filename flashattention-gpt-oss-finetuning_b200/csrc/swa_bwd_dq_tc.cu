@@ -418,6 +418,7 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
               // fma / sub / mul)
               const float2 sl2v = make_float2(sl2, sl2), nlse = make_float2(-lse_r, -lse_r);
               const float2 ndl = make_float2(-dl_r, -dl_r);
+              const uint32_t vm = full ? 0xffffu : vis_bits32(c_lo, min(c_hi, c_end - 1), c_sk);
               uint32_t dw[8];
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
@@ -425,9 +426,8 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
                 const float2 pr = make_float2(fast_exp2(t.x), fast_exp2(t.y));
                 float2 ds = __fmul2_rn(pr, __fadd2_rn(make_float2(dp[2 * e], dp[2 * e + 1]), ndl));
                 if (!full) {
-                  const int c = 2 * e;
-                  ds.x = (c < c_end && c <= c_hi && (c >= c_lo || c < c_sk)) ? ds.x : 0.f;
-                  ds.y = (c + 1 < c_end && c + 1 <= c_hi && (c + 1 >= c_lo || c + 1 < c_sk)) ? ds.y : 0.f;
+                  ds.x = (vm & (1u << (2 * e))) ? ds.x : 0.f;
+                  ds.y = (vm & (2u << (2 * e))) ? ds.y : 0.f;
                 }
                 dw[e] = Pack<T>::pack(ds.x, ds.y);
               }

@@ -352,6 +352,7 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
             // query i = qc0 + c sees key j iff c >= c_min and (c < c_max or j < S)
             const int c_min = j - qc0;
             const int c_max = (W > 0 && j >= S) ? j + W - qc0 : (j < S ? 1 << 30 : -(1 << 30));
+            const uint32_t vm = vis_bits32(c_min, c_max - 1, 0);
             // two columns per step on the packed fp32 pipe (same roundings as the scalar
             // fma / sub / mul)
             const float2 sl2v = make_float2(sl2, sl2);
@@ -362,8 +363,8 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
               const float2 t = __ffma2_rn(make_float2(s[c], s[c + 1]), sl2v, make_float2(-lse_s[c], -lse_s[c + 1]));
               float2 pr = make_float2(fast_exp2(t.x), fast_exp2(t.y));
               if (!full) {
-                pr.x = (c >= c_min && c < c_max) ? pr.x : 0.f;
-                pr.y = (c + 1 >= c_min && c + 1 < c_max) ? pr.y : 0.f;
+                pr.x = (vm & (1u << c)) ? pr.x : 0.f;
+                pr.y = (vm & (2u << c)) ? pr.y : 0.f;
               }
               const float2 dv = __fmul2_rn(pr, __fadd2_rn(make_float2(dp[c], dp[c + 1]),
                                                           make_float2(-dl_s[c], -dl_s[c + 1])));

@@ -317,6 +317,16 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // 2^x on the special-function unit (ex2.approx, flushes denormal results to zero).
+// Visibility of 32 consecutive key (or query) columns c = 0..31 for one thread's row, as a bit
+// mask: bit c is set iff c <= hi and (c >= lo or c < sk) (bounds relative to column 0, any
+// int).  Masking a column then costs one bit test instead of two or three compares.
+__device__ __forceinline__ uint32_t vis_bits32(int lo, int hi, int sk) {
+  const uint32_t upto_hi = hi >= 31 ? 0xffffffffu : (hi < 0 ? 0u : (2u << hi) - 1u);
+  const uint32_t from_lo = lo <= 0 ? 0xffffffffu : (lo > 31 ? 0u : ~((1u << lo) - 1u));
+  const uint32_t sinks = sk <= 0 ? 0u : (sk >= 32 ? 0xffffffffu : (1u << sk) - 1u);
+  return upto_hi & (from_lo | sinks);
+}
+
 // Three-input max / min (one sm_100 instruction each; NaN handling as max.f32 / min.f32).
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float r;

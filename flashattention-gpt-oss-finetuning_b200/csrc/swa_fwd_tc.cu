@@ -66,13 +66,11 @@ template <int N>
 __device__ __forceinline__ float mask_and_max(float* s, bool full, int c_lo, int c_hi, int c_sk,
                                               bool pos, float NEG, float sl2) {
   if (!full) {
-    if (c_sk <= 0) {
+    uint32_t vm[(N + 31) / 32];
 #pragma unroll
-      for (int c = 0; c < N; ++c) s[c] = (c >= c_lo && c <= c_hi) ? s[c] : NEG;
-    } else {
+    for (int w = 0; w < (N + 31) / 32; ++w) vm[w] = vis_bits32(c_lo - 32 * w, c_hi - 32 * w, c_sk - 32 * w);
 #pragma unroll
-      for (int c = 0; c < N; ++c) s[c] = (c <= c_hi && (c >= c_lo || c < c_sk)) ? s[c] : NEG;
-    }
+    for (int c = 0; c < N; ++c) s[c] = (vm[c / 32] & (1u << (c % 32))) ? s[c] : NEG;
   }
   float r;
   if constexpr (N >= 16) {
