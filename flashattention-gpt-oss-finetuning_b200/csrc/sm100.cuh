@@ -124,6 +124,13 @@ __device__ __forceinline__ void bulk_wait_read_all() {
 // Wait until all committed bulk stores have completed.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // Named barrier over `count` threads (ids 1..15; 0 is __syncthreads).
+// Programmatic dependent launch.  pdl_wait: block until the grid this launch depends on has
+// completed and its memory is visible (a no-op for a launch without the PDL attribute).
+// pdl_trigger: allow the next PDL launch in the stream to start (its CTAs take SMs as ours
+// leave; it still waits in its own pdl_wait before reading what this grid writes).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }

@@ -123,6 +123,10 @@ __global__ void __launch_bounds__(256 + 128 * SWA_DQ_NGRP, 1) bwd_dq_tc_kernel(c
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
+  // inputs may come from the previous launch in the stream (PDL): wait for it, then let the
+  // next launch start filling SMs as this grid's CTAs leave
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -480,8 +484,7 @@ cudaError_t launch_bwd_dq_tc(const BwdParams& p0, cudaStream_t st, int* err) {
   const int n_items = p.B * p.Hq * ((p.L + C::BM - 1) / C::BM);
   const int grid = persistent_grid(kern, C::THREADS, C::SMEM, C::TMEM_COLS, n_items);
   if (grid <= 0) return cudaErrorInvalidConfiguration;
-  kern<<<grid, C::THREADS, C::SMEM, st>>>(tm, p, err);
-  return cudaGetLastError();
+  return launch_pdl(kern, grid, C::THREADS, C::SMEM, st, tm, p, err);
 }
 
 #define SWA_INST(T, D) template cudaError_t launch_bwd_dq_tc<T, D>(const BwdParams&, cudaStream_t, int*);

@@ -338,6 +338,11 @@ __global__ void __launch_bounds__(192, 1) bwd_sink_far_kernel(const __grid_const
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+  // This grid reads only what the forward and the dQ pass wrote (both complete before the
+  // dK/dV grid, launched just before this one, passed its pdl_wait and let this grid start),
+  // so it runs beside the dK/dV grid's last CTAs; it waits for that grid before it completes,
+  // so that launches after this one (the sink-row reduction) see the dK/dV results too.
+  pdl_wait();
 }
 
 template <typename T, int D>
@@ -363,8 +368,7 @@ cudaError_t launch_sink_far(const BwdParams& p, cudaStream_t st, int* err) {
     const int n_units = p.B * p.Hkv * p.fk_u;
     const int grid = persistent_grid(kern, C::THREADS, C::SMEM, C::TMEM_COLS, n_units);
     if (grid <= 0) return cudaErrorInvalidConfiguration;
-    kern<<<grid, C::THREADS, C::SMEM, st>>>(tm, p, err);
-    return cudaGetLastError();
+    return launch_pdl(kern, grid, C::THREADS, C::SMEM, st, tm, p, err);
   }
 }
 

@@ -167,6 +167,10 @@ __global__ void __launch_bounds__(640, 1) bwd_dkdv_tc_kernel(const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
+  // inputs may come from the previous launch in the stream (PDL): wait for it, then let the
+  // next launch start filling SMs as this grid's CTAs leave
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer (whole warp)
@@ -463,6 +467,7 @@ __host__ __device__ inline int reduce_rows(const BwdParams& p) { return p.S < p.
 template <typename T, int D>
 __global__ void __launch_bounds__(32 * kReduceWarps) bwd_sink_reduce_kernel(BwdParams p) {
   __shared__ float part_sum[kReduceWarps][32];
+  pdl_wait();  // the partial slots come from the dK/dV and far sink-pair grids
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rows = reduce_rows(p);
   const int n_out = 2 * rows * D;
@@ -511,8 +516,7 @@ template <typename T, int D>
 cudaError_t launch_sink_reduce(const BwdParams& p, cudaStream_t st) {
   const long long n = (long long)p.B * p.Hkv * p.nst * ((2 * reduce_rows(p) * D + 31) / 32);
   if (n == 0) return cudaSuccess;
-  bwd_sink_reduce_kernel<T, D><<<(unsigned)n, 32 * kReduceWarps, 0, st>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(bwd_sink_reduce_kernel<T, D>, (int)n, 32 * kReduceWarps, 0, st, p);
 }
 
 template <typename T, int D> cudaError_t launch_sink_far(const BwdParams& p, cudaStream_t st, int* err);
@@ -537,8 +541,7 @@ cudaError_t launch_bwd_dkdv_tc(const BwdParams& p, cudaStream_t st, int* err) {
   const int n_items = p.B * p.Hkv * (p.nst * p.nc + n_kt);
   const int grid = persistent_grid(kern, C::THREADS, C::SMEM, C::TMEM_COLS, n_items);
   if (grid <= 0) return cudaErrorInvalidConfiguration;
-  kern<<<grid, C::THREADS, C::SMEM, st>>>(tm, p, err);
-  e = cudaGetLastError();
+  e = launch_pdl(kern, grid, C::THREADS, C::SMEM, st, tm, p, err);
   if (e != cudaSuccess || p.nst == 0) return e;
   if (p.fk_c > 0 && (e = launch_sink_far<T, D>(p, st, err)) != cudaSuccess) return e;
   return launch_sink_reduce<T, D>(p, st);

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "swa_attn.h"
 
 namespace swa {
@@ -360,6 +362,25 @@ __device__ __forceinline__ void load_tile_async(T* smem, const T* gbase, int64_t
     const T* src = gbase + (int64_t)(ok ? gr : 0) * ld + ch * 8;
     cp_async16(smem_u32(smem + r * PITCH + ch * 8), src, ok ? 16 : 0);
   }
+}
+
+// Launch with programmatic stream serialisation: the kernel may start while the previous
+// kernel in the stream drains (every kernel launched this way calls pdl_wait before touching
+// memory that an earlier launch writes).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, int smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)block);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // Number of CTAs for a persistent kernel: resident CTAs per SM (limited by registers,

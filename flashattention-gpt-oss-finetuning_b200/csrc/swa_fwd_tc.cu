@@ -223,6 +223,10 @@ __global__ void __launch_bounds__(224, D <= 64 ? 2 : 1) fwd_tc_kernel(const __gr
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
+  // inputs may come from the previous launch in the stream (PDL): wait for it, then let the
+  // next launch start filling SMs as this grid's CTAs leave
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -508,8 +512,7 @@ cudaError_t launch_fwd_tc(const FwdParams& p0, cudaStream_t st, int* err) {
   const int n_items = p.B * p.Hq * ((p.L + C::BM - 1) / C::BM);
   const int grid = persistent_grid(kern, 224, C::SMEM, C::TMEM_COLS, n_items);
   if (grid <= 0) return cudaErrorInvalidConfiguration;
-  kern<<<grid, 224, C::SMEM, st>>>(tm, p, err);
-  return cudaGetLastError();
+  return launch_pdl(kern, grid, 224, C::SMEM, st, tm, p, err);
 }
 
 #define SWA_INST(T, D) template cudaError_t launch_fwd_tc<T, D>(const FwdParams&, cudaStream_t, int*);
