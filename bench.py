@@ -8,10 +8,10 @@ Metric: effective TFLOP/s of fwd+bwd counting only useful (window + sink) FLOPs
 (14 * D per visible (query, key) pair), whole job over all ranks.  Work is partitioned by
 independent (batch, KV head) units with no collective on the data path; the barrier and the
 max-over-ranks device time are the only cross-rank traffic.
-  --scaling weak   (default) every rank runs its own full copy of the workload's shape
-                   (global batch = N x B);
-  --scaling strong the workload is fixed and its units are split over the ranks (e.g.
-                   cfg4_long_swa: 8 KV heads over 1/2/4/8 GPUs).
+  --scaling strong (default) the workload is fixed and its (batch, KV head) units are split
+                   over the ranks (cfg2: 32 units, 4 per GPU at N = 8);
+  --scaling weak   every rank runs its own full copy of the workload's shape
+                   (global batch = N x B).
   --scaling seq    the workload is fixed and its sequence is split over the ranks
                    (seqsplit.py: K/V halo and sink rows exchanged over NCCL inside the timed
                    step, halo dK/dV and sink partials sent back).
@@ -175,6 +175,22 @@ def run_reference(args, w, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_reference_triton(args, w, rank, local_rank):
+    """One line for the reference's Triton kernels on one GPU (rank 0 only)."""
+    if rank != 0:
+        return
+    line = {"impl": "reference_triton", "metric": METRIC, "unit": UNIT, "n_gpus": 1,
+            "higher_is_better": True, "config": w.describe()}
+    if not torch.cuda.is_available():
+        line["unavailable"] = "no CUDA device"
+    else:
+        dev = torch.device("cuda", local_rank)
+        torch.cuda.set_device(dev)
+        r = reference_triton_timed(w, dev, args.steps, args.warmup)
+        line.update(r)
+    print(json.dumps(line), flush=True)
+
+
 # ---------------------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------------------
@@ -295,6 +311,121 @@ def e2e_timed(w, dev, rank, steps, warmup):
     return a.elapsed_time(b), h2d, d2h
 
 
+def copy_floor_timed(w, dev, steps):
+    """The host link's own floor for the e2e step: the same pinned input bytes host->device on
+    one stream and the same output bytes device->host on another, both directions at once,
+    nothing else running.  Returns ms per step."""
+    qs = (w.batch, w.n_q_heads, w.seq_len, w.head_dim)
+    ks = (w.batch, w.n_kv_heads, w.seq_len, w.head_dim)
+    host_in = [torch.empty(sh, dtype=w.dtype).pin_memory() for sh in (qs, ks, ks, qs)]
+    host_out = [torch.empty(sh, dtype=w.dtype).pin_memory() for sh in (qs, qs, ks, ks)]
+    dev_in = [torch.empty(t.shape, dtype=t.dtype, device=dev) for t in host_in]
+    dev_out = [torch.empty(t.shape, dtype=t.dtype, device=dev) for t in host_out]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    main = torch.cuda.current_stream(dev)
+
+    def run(n):
+        s_in.wait_stream(main)
+        s_out.wait_stream(main)
+        for _ in range(n):
+            with torch.cuda.stream(s_in):
+                for d, h in zip(dev_in, host_in):
+                    d.copy_(h, non_blocking=True)
+            with torch.cuda.stream(s_out):
+                for h, d in zip(host_out, dev_out):
+                    h.copy_(d, non_blocking=True)
+        main.wait_stream(s_in)
+        main.wait_stream(s_out)
+
+    run(2)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(main)
+    run(steps)
+    b.record(main)
+    torch.cuda.synchronize(dev)
+    return a.elapsed_time(b) / steps
+
+
+def _load_reference_triton():
+    """The reference's own module (unmodified), installed under baseline/_ref, or the
+    directory named by SWA_REFERENCE_DIR.  Returns (module, None) or (None, reason)."""
+    import importlib.util
+    cands = [os.environ.get("SWA_REFERENCE_DIR"), os.path.join(ROOT, "baseline", "_ref")]
+    for d in cands:
+        if not d:
+            continue
+        path = os.path.join(d, "flash_attention_gpt_oss.py")
+        if os.path.exists(path):
+            try:
+                spec = importlib.util.spec_from_file_location("_reference_flash_attention_gpt_oss", path)
+                mod = importlib.util.module_from_spec(spec)
+                spec.loader.exec_module(mod)
+                return mod, None
+            except Exception as e:  # import error (e.g. no triton): reported, not raised
+                return None, f"importing the reference from {d} failed: {type(e).__name__}: {e}"
+    return None, ("the reference is not installed on this box (baseline/_ref is absent and "
+                  "SWA_REFERENCE_DIR is unset)")
+
+
+def reference_triton_timed(w, dev, steps, warmup):
+    """The reference's Triton kernels (FlashSWDAWithSink, flash_attention_gpt_oss.py:340-438)
+    on this GPU through its own autograd Function, fwd+bwd of ``w``, CUDA events on the
+    launching stream.  Returns a dict for the JSON line (or {"unavailable": reason})."""
+    mod, why = _load_reference_triton()
+    if mod is None:
+        return {"unavailable": why}
+    q, k, v, do = wl.make_inputs(w, device=dev)
+    qd, kd, vd = (t.detach().requires_grad_() for t in (q, k, v))
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for t in (qd, kd, vd):
+            t.grad = None
+        o = mod.flash_swda_with_sink(qd, kd, vd, w.window_size, w.sink_size)
+        o.backward(do)
+        return o
+
+    try:
+        for _ in range(warmup):
+            o = step()
+        torch.cuda.synchronize(dev)
+    except Exception as e:
+        return {"unavailable": f"the reference's Triton kernels failed here: {type(e).__name__}: "
+                               f"{str(e).splitlines()[0][:200] if str(e) else ''}"}
+    # the same inputs through this library's drop-in Function, for a sanity comparison
+    qo, ko, vo = (t.detach().clone().requires_grad_() for t in (q, k, v))
+    oo = PKG.flash_swda_with_sink(qo, ko, vo, w.window_size, w.sink_size)
+    oo.backward(do)
+    ours = (oo, qo.grad, ko.grad, vo.grad)
+    diffs = {}
+    for n, a, b in zip(("o", "dq", "dk", "dv"), (o, qd.grad, kd.grad, vd.grad), ours):
+        a, b = a.detach().float(), b.detach().float()
+        diffs[n] = (a - b).abs().max().item() / max(b.abs().max().item(), 1e-30)
+    del ours, oo, qo, ko, vo
+    a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a_ev.record(stream)
+    for _ in range(steps):
+        step()
+    b_ev.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = a_ev.elapsed_time(b_ev) / steps
+    return {"value": wl.useful_flops(w) / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
+            "steps": steps, "warmup": warmup,
+            "path": "reference FlashSWDAWithSink (Triton) from baseline/_ref, autograd fwd+bwd, "
+                    "inputs resident on the GPU, CUDA events",
+            "max_rel_diff_vs_ours": diffs}
+
+
+def gather_over_ranks(x: float, dev) -> list:
+    if not torch.distributed.is_initialized():
+        return [x]
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    out = [torch.zeros_like(t) for _ in range(torch.distributed.get_world_size())]
+    torch.distributed.all_gather(out, t)
+    return [float(o.item()) for o in out]
+
+
 def max_over_ranks(x: float, dev) -> float:
     if not torch.distributed.is_initialized():
         return x
@@ -324,6 +455,9 @@ def run_ours(args, w_job, rank, world, local_rank):
     total_ms, per_phase, launches, graph_ms = device_timed(w, dev, rank, args.steps, args.warmup)
     graph_ms = max_over_ranks(graph_ms, dev) / args.steps
     clk = clocks.stop() if clocks else None
+    per_rank_ms = [x / args.steps for x in gather_over_ranks(total_ms, dev)]
+    per_rank_units = [len(u) for u in sh_mod.plan_units(w_job.batch, w_job.n_kv_heads, world)] \
+        if args.scaling == "strong" else [w_job.batch * w_job.n_kv_heads] * world
     total_ms = max_over_ranks(total_ms, dev)
     ms = total_ms / args.steps
     flops_job = wl.useful_flops(w_job) * (world if args.scaling == "weak" else 1)
@@ -334,9 +468,15 @@ def run_ours(args, w_job, rank, world, local_rank):
         e_steps = max(3, min(args.steps, 10))
         e_ms, h2d, d2h = e2e_timed(w, dev, rank, e_steps, max(3, min(args.warmup, 3)))
         e_ms = max_over_ranks(e_ms, dev) / e_steps
+        floor_ms = max_over_ranks(copy_floor_timed(w, dev, e_steps), dev)
         e2e = {"value": flops_job / (e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e_ms,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "path": "flash_swda_with_sink autograd, pinned host in/out, copies overlapped across steps"}
+               "copy_floor_ms": floor_ms, "frac_of_copy_floor": floor_ms / e_ms,
+               "path": "flash_swda_with_sink autograd, pinned host in/out, copies overlapped across steps",
+               "copy_floor": "the same pinned bytes in and out on two streams at once, no compute"}
+    ref_triton = None
+    if world == 1 and not args.no_reference_triton:
+        ref_triton = reference_triton_timed(w, dev, max(3, min(args.steps, 10)), 3)
 
     if rank != 0:
         return
@@ -355,7 +495,9 @@ def run_ours(args, w_job, rank, world, local_rank):
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof.update(kernel=dom, peak_source=f"MEASURED_PEAKS.json burst ({peak_kind})",
                 algorithmic_flops=kw["flops"], algorithmic_bytes=kw["bytes"],
-                kernel_ms=per_phase[dom], traffic=TRAFFIC.get((w.name, dom)),
+                kernel_ms=per_phase[dom],
+                traffic=TRAFFIC.get((kernel_sources_sha(), w_job.name, dom)) if world == 1 else None,
+                kernel_sources_sha=kernel_sources_sha(),
                 tensor_frac=(kw["flops"] / t_s / 1e12) / tf_peak,
                 hbm_frac=(kw["bytes"] / t_s / 1e9) / hbm_peak)
     line = {
@@ -367,12 +509,14 @@ def run_ours(args, w_job, rank, world, local_rank):
                        per_rank=w.describe(), parallelism=f"dp{world} by (batch, kv_head) units",
                        l2="inputs larger than L2 (q, dO 134 MB each + k, v, o, grads)"),
         "phase_ms": per_phase,
+        "per_rank": {"ms_per_step": per_rank_ms, "units": per_rank_units},
         "gpu_launches": launches,
         "cuda_graph": {"ms_per_step": graph_ms, "value": flops_job / (graph_ms * 1e-3) / 1e12,
                        "note": "same step captured once (SwaPlan.capture) and replayed"},
         "roofline": roof,
         "clocks": clk,
         "e2e": e2e,
+        "reference_triton": ref_triton,
     }
     if world == 1 and not args.no_cpu_baseline:
         cb = cpu_sample_time(w, 3, 1)
@@ -518,10 +662,22 @@ def run_variant(args, w, local_rank):
     print(json.dumps(line), flush=True)
 
 
-# DRAM bytes (read + write) per step of a phase from one ncu capture, keyed by (workload,
-# phase): the dK/dV phase of cfg2 = dK/dV kernel 345.6 MB + far sink-pair kernel 261.0 MB
-# (profiles/step_cfg2_dram_traffic.md).
-TRAFFIC: dict = {("cfg2_gptoss_swa", "bwd_dkdv"): 322_498_560 + 23_117_824 + 259_731_712 + 1_313_792}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum, summed over the phase's kernels)
+# per step of a phase, from one ncu capture of `bench.py --steps 1 --warmup 3`, keyed by
+# (hash of the kernel sources, workload, phase).  A figure taken on other kernel sources is
+# never reported: the line then carries traffic = null.
+TRAFFIC: dict = {}
+
+
+def kernel_sources_sha() -> str:
+    import hashlib
+    csrc = os.path.join(ROOT, "flashattention-gpt-oss-finetuning_b200", "csrc")
+    h = hashlib.sha256()
+    for name in sorted(os.listdir(csrc)):
+        if name.endswith((".cu", ".cuh", ".h")):
+            with open(os.path.join(csrc, name), "rb") as f:
+                h.update(name.encode() + b"\0" + f.read())
+    return h.hexdigest()[:12]
 
 
 def main():
@@ -529,13 +685,16 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference_triton"], default="ours",
+                    help="reference: the CPU reference arm; reference_triton: the reference's "
+                         "Triton kernels on one GPU (the second comparison point)")
     ap.add_argument("--workload", default="cfg2_gptoss_swa", choices=sorted(wl.CONFIGS))
-    ap.add_argument("--scaling", choices=["weak", "strong", "seq"], default="weak")
+    ap.add_argument("--scaling", choices=["weak", "strong", "seq"], default="strong")
     ap.add_argument("--variant", choices=["plain", "sink_logits", "varlen"], default="plain",
                     help="additional modes, 1 GPU (default: the headline path)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-triton", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -545,6 +704,9 @@ def main():
     w = wl.CONFIGS[args.workload]
     if args.impl == "reference":
         run_reference(args, w, rank, world)
+        return
+    if args.impl == "reference_triton":
+        run_reference_triton(args, w, rank, local_rank)
         return
     if world > 1:
         torch.cuda.set_device(local_rank)

@@ -31,6 +31,7 @@ EXPORTED_SYMBOLS = (
     "swa_status_string", "swa_last_cuda_error", "swa_version", "swa_lse_row_stride",
     "swa_selftest_wait_timeout", "swa_fwd_sink_logits", "swa_bwd_sink_logits",
     "swa_varlen_lse_floats", "swa_varlen_bwd_workspace_size", "swa_varlen_fwd", "swa_varlen_bwd",
+    "swa_device_status_async",
 )
 
 
@@ -134,6 +135,8 @@ def _declare(l):
     l.swa_status_string.restype = ctypes.c_char_p
     l.swa_last_cuda_error.argtypes = []
     l.swa_last_cuda_error.restype = ctypes.c_char_p
+    l.swa_device_status_async.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+    l.swa_device_status_async.restype = ctypes.c_int
     l.swa_selftest_wait_timeout.argtypes = [ctypes.c_int, ctypes.c_void_p]
     l.swa_selftest_wait_timeout.restype = ctypes.c_int
     l.swa_lse_row_stride.argtypes = [ctypes.c_int]
@@ -171,3 +174,81 @@ def check(status: int, where: str):
         detail = lib().swa_last_cuda_error().decode()
     cls = SwaDeviceTimeout if status == SWA_ERR_DEVICE_TIMEOUT else SwaError
     raise cls(status, where, detail)
+
+
+# ---------------------------------------------------------------------------------------
+# Timeout monitor: surfaces an on-device wait that gave up without synchronising each call.
+#
+# After every launch sequence the Python API enqueues (swa_device_status_async) a copy of the
+# device's error flag into a pinned host word and records an event behind it.  The next call
+# on that device first looks at the word if the event has completed: a set flag means that an
+# earlier launch's outputs are invalid (and that the kernels skip their work until the flag is
+# cleared), so the call clears it (swa_check_device, which synchronises) and raises
+# SwaDeviceTimeout instead of returning zeros.  Nothing is enqueued while a stream is being
+# captured into a CUDA graph.
+# ---------------------------------------------------------------------------------------
+
+class _Monitor:
+    def __init__(self, dev):
+        import torch
+        self.flag = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.event = torch.cuda.Event()
+        self.armed = False
+        self.dev = dev
+
+
+_monitors = {}
+
+
+def _monitor(dev):
+    m = _monitors.get(dev.index)
+    if m is None:
+        with _lock:
+            m = _monitors.get(dev.index)
+            if m is None:
+                m = _monitors[dev.index] = _Monitor(dev)
+    return m
+
+
+def _capturing(dev) -> bool:
+    import torch
+    return torch.cuda.is_current_stream_capturing()
+
+
+def raise_if_device_timed_out(dev, stream_handle: int, where: str):
+    """Raise SwaDeviceTimeout when a launch polled earlier on ``dev`` has reported a timeout."""
+    if _capturing(dev):
+        return
+    m = _monitor(dev)
+    if not m.armed or not m.event.query():
+        return
+    m.armed = False
+    if int(m.flag[0]) == 0:
+        return
+    m.flag[0] = 0
+    lib().swa_check_device(stream_handle)  # synchronises and clears the device flag
+    raise SwaDeviceTimeout(SWA_ERR_DEVICE_TIMEOUT, where,
+                           "an on-device wait of an earlier launch on this device gave up; "
+                           "that launch's outputs are invalid")
+
+
+def poll_device_status(dev, stream):
+    """Enqueue the error-flag copy behind the launches just made on ``stream``."""
+    if _capturing(dev):
+        return
+    m = _monitor(dev)
+    check(lib().swa_device_status_async(m.flag.data_ptr(), stream.cuda_stream),
+          "swa_device_status_async")
+    m.event.record(stream)
+    m.armed = True
+
+
+def selftest_wait_timeout(limit_us: int, dev, stream=None):
+    """Launch the failure-path self-test kernel (a bounded wait that gives up after
+    ``limit_us``) and poll its status like any API call, so the next API call on ``dev``
+    raises SwaDeviceTimeout."""
+    import torch
+    st = stream or torch.cuda.current_stream(dev)
+    check(lib().swa_selftest_wait_timeout(int(limit_us), st.cuda_stream),
+          "swa_selftest_wait_timeout")
+    poll_device_status(dev, st)

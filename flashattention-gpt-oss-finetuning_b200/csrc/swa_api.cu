@@ -214,6 +214,14 @@ int swa_check_device(void* stream) {
   return SWA_ERR_DEVICE_TIMEOUT;
 }
 
+int swa_device_status_async(int* host_flag, void* stream) {
+  if (!host_flag) return SWA_ERR_INVALID_ARG;
+  int* err = device_error_ptr();
+  if (!err) return SWA_ERR_LAUNCH;
+  return record(cudaMemcpyAsync(host_flag, err, sizeof(int), cudaMemcpyDeviceToHost,
+                                static_cast<cudaStream_t>(stream)));
+}
+
 int swa_selftest_wait_timeout(int limit_us, void* stream) {
   if (limit_us <= 0 || limit_us > 1000000) return SWA_ERR_INVALID_ARG;
   int* err = device_error_ptr();

@@ -1,5 +1,5 @@
-// swa_common.cuh -- shared device helpers: visibility rule, key-tile schedules, warp-level
-// MMA / ldmatrix / cp.async wrappers and fast exp2.
+// swa_common.cuh -- shared device helpers: visibility rule, item and key-segment schedules,
+// the sink-key split of the dK/dV pass, element packing, fast exp2 and launch helpers.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -45,52 +45,6 @@ __device__ __forceinline__ bool block_none_visible(int r0, int r1, int c0, int c
   if (c0 > r1 - 1) return true;                         // every key after every row
   if (c0 >= S && r0 - (c1 - 1) >= W) return true;       // outside the window, no sinks
   return false;
-}
-
-// ---------------------------------------------------------------------------------------
-// Key-tile schedule of one query tile [q0, q0 + BM) with BN-wide key tiles: the sink tiles
-// that lie below the window, then the window tiles.  Only these tiles are touched.
-// ---------------------------------------------------------------------------------------
-struct KeySchedule {
-  int n_sink;   // sink tiles 0 .. n_sink-1
-  int win_lo;   // first window tile
-  int n_total;  // n_sink + window tiles
-  __device__ __forceinline__ int tile(int it) const { return it < n_sink ? it : win_lo + (it - n_sink); }
-};
-
-__device__ __forceinline__ KeySchedule key_schedule(int q0, int BM, int BN, int L, int W, int S) {
-  KeySchedule ks;
-  int q_last = min(q0 + BM, L) - 1;
-  int lo = q0 - (W - 1);
-  if (lo < 0) lo = 0;
-  if (W <= 0) lo = q_last + 1;              // no window: only sinks
-  int win_lo = lo / BN;
-  int win_hi = (W <= 0) ? win_lo - 1 : q_last / BN;   // inclusive
-  if (W <= 0) win_lo = win_hi + 1;
-  int sink_keys = min(S, q_last + 1);
-  int n_sink = (sink_keys + BN - 1) / BN;
-  if (W > 0 && n_sink > win_lo) n_sink = win_lo;
-  ks.n_sink = n_sink;
-  ks.win_lo = win_lo;
-  ks.n_total = n_sink + ((win_hi >= win_lo) ? (win_hi - win_lo + 1) : 0);
-  return ks;
-}
-
-// Query tiles that see any key of the key tile [k0, k0 + BN): [qt_lo, qt_hi).
-__device__ __forceinline__ void query_range(int k0, int BN, int BM, int L, int W, int S,
-                                            int* qt_lo, int* qt_hi) {
-  int n_qt = (L + BM - 1) / BM;
-  *qt_lo = k0 / BM;
-  int k_last = min(k0 + BN, L) - 1;
-  if (k0 < S) {
-    *qt_hi = n_qt;
-  } else if (W <= 0) {
-    *qt_hi = *qt_lo;
-  } else {
-    long long last_row = (long long)k_last + W - 1;   // farthest query that still sees k_last
-    if (last_row > L - 1) last_row = L - 1;
-    *qt_hi = (int)(last_row / BM) + 1;
-  }
 }
 
 // ---------------------------------------------------------------------------------------
@@ -271,54 +225,6 @@ template <> struct Pack<__nv_bfloat16> {
   static __device__ __forceinline__ float to(__nv_bfloat16 a) { return __bfloat162float(a); }
 };
 
-// D(16x8, f32) += A(16x16) * B(16x8), warp-wide.
-template <typename T>
-__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1);
-template <>
-__device__ __forceinline__ void mma16816<__half>(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-template <>
-__device__ __forceinline__ void mma16816<__nv_bfloat16>(float* c, const uint32_t* a, uint32_t b0,
-                                                        uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t* r, uint32_t addr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t* r, uint32_t addr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-
-// 16-byte async global->shared copy; src_bytes = 0 zero-fills the destination.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src),
-               "r"(src_bytes));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
-}
-
-// 2^x on the special-function unit (ex2.approx, flushes denormal results to zero).
 // Visibility of 32 consecutive key (or query) columns c = 0..31 for one thread's row, as a bit
 // mask: bit c is set iff c <= hi and (c >= lo or c < sk) (bounds relative to column 0, any
 // int).  Masking a column then costs one bit test instead of two or three compares.
@@ -341,27 +247,11 @@ __device__ __forceinline__ float min3f(float a, float b, float c) {
   return r;
 }
 
+// 2^x on the special-function unit (ex2.approx, flushes denormal results to zero).
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
   return y;
-}
-
-// Load a [rows x D] tile of a [.., L, D] tensor (row stride `ld` elements) into shared memory
-// with a padded row pitch of D + 8 elements.  Rows >= L are zero-filled.
-template <typename T, int D, int ROWS, int NTHREADS>
-__device__ __forceinline__ void load_tile_async(T* smem, const T* gbase, int64_t ld, int row0,
-                                                int L, int tid) {
-  constexpr int CH = D / 8;  // 16-byte chunks per row
-  constexpr int PITCH = D + 8;
-#pragma unroll
-  for (int c = tid; c < ROWS * CH; c += NTHREADS) {
-    int r = c / CH, ch = c % CH;
-    int gr = row0 + r;
-    bool ok = gr < L;
-    const T* src = gbase + (int64_t)(ok ? gr : 0) * ld + ch * 8;
-    cp_async16(smem_u32(smem + r * PITCH + ch * 8), src, ok ? 16 : 0);
-  }
 }
 
 // Launch with programmatic stream serialisation: the kernel may start while the previous

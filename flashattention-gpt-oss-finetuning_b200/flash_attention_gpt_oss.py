@@ -128,12 +128,14 @@ def swa_forward(q, k, v, window_size: int, sink_size: int = 0,
     args = _lib.SwaFwdArgs(_problem(q, k, window_size, sink_size, softmax_scale, dk_),
                            _tensor(qp), _tensor(kp), _tensor(vp), _tensor(o), lse.data_ptr())
     with torch.cuda.device(q.device):
+        _lib.raise_if_device_timed_out(q.device, _stream(q.device), "swa_fwd")
         if sink_logits is None:
             _lib.check(_lib.lib().swa_fwd(ctypes.byref(args), _stream(q.device)), "swa_fwd")
         else:
             sl = _sink_logits_f32(sink_logits, q)
             _lib.check(_lib.lib().swa_fwd_sink_logits(ctypes.byref(args), sl.data_ptr(),
                                                       _stream(q.device)), "swa_fwd_sink_logits")
+        _lib.poll_device_status(q.device, torch.cuda.current_stream(q.device))
     if dk_ != d:
         o = o[..., :d]
     return o, lse[..., :l]
@@ -166,6 +168,7 @@ def swa_backward(q, k, v, o, lse, do, window_size: int, sink_size: int = 0,
                            ws.data_ptr(), ws_bytes)
     dsl = None
     with torch.cuda.device(q.device):
+        _lib.raise_if_device_timed_out(q.device, _stream(q.device), "swa_bwd")
         if sink_logits is None:
             _lib.check(lib.swa_bwd(ctypes.byref(args), _stream(q.device)), "swa_bwd")
         else:
@@ -173,6 +176,7 @@ def swa_backward(q, k, v, o, lse, do, window_size: int, sink_size: int = 0,
             dsl = torch.empty_like(sl)
             _lib.check(lib.swa_bwd_sink_logits(ctypes.byref(args), sl.data_ptr(), dsl.data_ptr(),
                                                _stream(q.device)), "swa_bwd_sink_logits")
+        _lib.poll_device_status(q.device, torch.cuda.current_stream(q.device))
     if dk_ != d:
         dq, dk, dv = dq[..., :d], dk[..., :d], dv[..., :d]
     return (dq, dk, dv) if dsl is None else (dq, dk, dv, dsl)

@@ -79,9 +79,13 @@ class SwaPlan:
         self.bwd_dkdv(stream)
 
     def step(self, stream=None):
-        """One forward + backward over the bound buffers."""
-        self.fwd(stream)
-        self.bwd(stream)
+        """One forward + backward over the bound buffers.  Raises SwaDeviceTimeout when an
+        earlier step's on-device wait gave up (polled without a host synchronisation)."""
+        st = stream or torch.cuda.current_stream(self.device)
+        _lib.raise_if_device_timed_out(self.device, st.cuda_stream, "SwaPlan.step")
+        self.fwd(st)
+        self.bwd(st)
+        _lib.poll_device_status(self.device, st)
 
     def capture(self) -> "torch.cuda.CUDAGraph":
         """Record one forward + backward (``step``) into a CUDA graph over the bound buffers.

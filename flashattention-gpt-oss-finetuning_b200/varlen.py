@@ -95,7 +95,9 @@ def swa_varlen_forward(q, k, v, cu_seqlens: CuSeqlens, window_size: int, sink_si
     args = _lib.SwaVarlenFwdArgs(prob, cu.ctypes.data, _packed(qp), _packed(kp), _packed(vp),
                                  _packed(o), lse.data_ptr(), None if sl is None else sl.data_ptr())
     with torch.cuda.device(q.device):
+        _lib.raise_if_device_timed_out(q.device, _stream(q.device), "swa_varlen_fwd")
         _lib.check(lib.swa_varlen_fwd(ctypes.byref(args), _stream(q.device)), "swa_varlen_fwd")
+        _lib.poll_device_status(q.device, torch.cuda.current_stream(q.device))
     if dk_ != d:
         o = o[..., :d]
     return o, lse, cu
@@ -134,7 +136,9 @@ def swa_varlen_backward(q, k, v, o, lse, cu: np.ndarray, do, window_size: int,
                                  _packed(dk), _packed(dv), None if sl is None else sl.data_ptr(),
                                  None if dsl is None else dsl.data_ptr(), ws.data_ptr(), ws_bytes)
     with torch.cuda.device(q.device):
+        _lib.raise_if_device_timed_out(q.device, _stream(q.device), "swa_varlen_bwd")
         _lib.check(lib.swa_varlen_bwd(ctypes.byref(args), _stream(q.device)), "swa_varlen_bwd")
+        _lib.poll_device_status(q.device, torch.cuda.current_stream(q.device))
     if dk_ != d:
         dq, dk, dv = dq[..., :d], dk[..., :d], dv[..., :d]
     return (dq, dk, dv) if dsl is None else (dq, dk, dv, dsl)

@@ -216,6 +216,14 @@ SWA_API int swa_bwd_no_alloc(const SwaBwdArgs* args, void* stream);
  * (that launch's outputs are then undefined), SWA_OK otherwise. */
 SWA_API int swa_check_device(void* stream);
 
+/* Enqueue on `stream` a copy of the current device's on-device error flag into
+ * `*host_flag` (host memory, preferably pinned so the copy stays asynchronous) and return
+ * without waiting.  Once the stream has passed that point, *host_flag != 0 means that a
+ * bounded wait of some earlier launch gave up (its outputs are undefined, and later launches
+ * skip their work until swa_check_device clears the flag).  Lets a host poll for timeouts
+ * without synchronising every call.  No counterpart in the reference. */
+SWA_API int swa_device_status_async(int* host_flag, void* stream);
+
 /* Failure-path self-test: launches a kernel whose bounded on-device wait (on a barrier that
  * nothing arrives at) gives up after `limit_us` microseconds (1 .. 1e6) and records the
  * error; a following swa_check_device returns SWA_ERR_DEVICE_TIMEOUT.  No counterpart in the
