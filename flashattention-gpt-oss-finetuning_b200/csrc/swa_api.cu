@@ -1,6 +1,7 @@
 // swa_api.cu -- the extern "C" entry points declared in include/swa_attn.h: argument
 // validation (the checks of flash_attention_gpt_oss.py:343-354 plus the layout
 // requirements of these kernels), dtype/head-dim dispatch and error reporting.
+#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
@@ -11,6 +12,7 @@
 
 namespace swa {
 template <typename T, int D> cudaError_t launch_fwd_tc(const FwdParams&, cudaStream_t, int*);
+template <typename T, int D> cudaError_t launch_fwd_gqa(const FwdParams&, cudaStream_t, int*, bool*);
 cudaError_t launch_selftest_wait_timeout(int* err, unsigned long long limit_ns, cudaStream_t st);
 cudaError_t launch_sink_logit_grad(const float* lse, const float* delta, const float* sinks,
                                    float* dsinks, int B, int Hq, int lse_ld, bool accumulate,
@@ -110,8 +112,23 @@ int dispatch(const SwaProblem& pr, const P& kp, cudaStream_t st) {
   return record(e);
 }
 
+// SWA_FWD_PER_HEAD=1 in the environment turns the GQA-packed forward off (every problem then
+// takes the per-head forward); read once.
+bool gqa_forward_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("SWA_FWD_PER_HEAD");
+    return !(v && v[0] == '1');
+  }();
+  return on;
+}
+
 template <typename T, int D> struct Fwd {
   static cudaError_t run(const swa::FwdParams& p, cudaStream_t s) {
+    if (gqa_forward_enabled()) {
+      bool used = false;
+      cudaError_t e = swa::launch_fwd_gqa<T, D>(p, s, device_error_ptr(), &used);
+      if (used || e != cudaSuccess) return e;
+    }
     return swa::launch_fwd_tc<T, D>(p, s, device_error_ptr());
   }
 };

@@ -37,10 +37,12 @@ inline CUtensorMapSwizzle swizzle_for_row_bytes(int row_bytes) {
 }
 
 // Tensor map over a [B, H, L, D] 16-bit tensor (element strides sb, sh, sl; dim 3 stride 1).
-// Box: {box_d, box_rows, 1, 1}; swizzle width = box_d * 2 bytes (32, 64 or 128).
-// Rows past L (and any other out-of-range coordinate) read as zero.
+// Box: {box_d, box_rows, box_heads, 1}; swizzle width = box_d * 2 bytes (32, 64 or 128).
+// Rows past L (and any other out-of-range coordinate) read as zero.  A box of several heads
+// lands in shared memory as [box_heads][box_rows][box_d].
 inline bool make_tmap_bhld(CUtensorMap* m, const void* base, int B, int H, int L, int D,
-                           int64_t sb, int64_t sh, int64_t sl, int box_d, int box_rows) {
+                           int64_t sb, int64_t sh, int64_t sl, int box_d, int box_rows,
+                           int box_heads = 1) {
   EncodeTiledFn fn = encode_tiled_fn();
   if (!fn) return false;
   const int64_t e = 2;
@@ -49,7 +51,7 @@ inline bool make_tmap_bhld(CUtensorMap* m, const void* base, int B, int H, int L
   if (B == 1) sb = sh * H;
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)L, (cuuint64_t)H, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)(sl * e), (cuuint64_t)(sh * e), (cuuint64_t)(sb * e)};
-  cuuint32_t box[4] = {(cuuint32_t)box_d, (cuuint32_t)box_rows, 1, 1};
+  cuuint32_t box[4] = {(cuuint32_t)box_d, (cuuint32_t)box_rows, (cuuint32_t)box_heads, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for_row_bytes(box_d * 2),
