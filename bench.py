@@ -175,6 +175,25 @@ def run_reference(args, w, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_profile_phase(args, w, local_rank):
+    """Run one phase of the workload alone, for a profiler to capture."""
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    q, k, v, do = wl.make_inputs(w, device=dev)
+    plan = plan_mod.SwaPlan(q, k, v, w.window_size, w.sink_size, None, dout=do)
+    for _ in range(args.warmup):
+        plan.step()
+    fn = {"fwd": plan.fwd, "bwd_dq": plan.bwd_dq, "bwd_dkdv": plan.bwd_dkdv}[args.profile_phase]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"profile_phase": args.profile_phase, "workload": w.name,
+                      "ms_per_launch_set": e0.elapsed_time(e1) / args.steps}), flush=True)
+
+
 def run_reference_triton(args, w, rank, local_rank):
     """One line for the reference's Triton kernels on one GPU (rank 0 only)."""
     if rank != 0:
@@ -695,6 +714,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-triton", action="store_true")
+    ap.add_argument("--profile-phase", choices=["fwd", "bwd_dq", "bwd_dkdv"], default=None,
+                    help="profiling driver: `--warmup` full steps, then `--steps` launches of "
+                         "this phase only (for an ncu capture with -k / -s / -c); prints one line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -704,6 +726,9 @@ def main():
     w = wl.CONFIGS[args.workload]
     if args.impl == "reference":
         run_reference(args, w, rank, world)
+        return
+    if args.profile_phase:
+        run_profile_phase(args, w, local_rank)
         return
     if args.impl == "reference_triton":
         run_reference_triton(args, w, rank, local_rank)
