@@ -19,6 +19,7 @@ cudaError_t launch_sink_logit_grad(const float* lse, const float* delta, const f
                                    cudaStream_t st);
 template <typename T, int D> cudaError_t launch_bwd_preprocess(const BwdParams&, cudaStream_t);
 template <typename T, int D> cudaError_t launch_bwd_dq_tc(const BwdParams&, cudaStream_t, int*);
+template <typename T, int D> cudaError_t launch_bwd_dq_gqa(const BwdParams&, cudaStream_t, int*, bool*);
 template <typename T, int D> cudaError_t launch_bwd_dkdv_tc(const BwdParams&, cudaStream_t, int*);
 }  // namespace swa
 
@@ -112,8 +113,8 @@ int dispatch(const SwaProblem& pr, const P& kp, cudaStream_t st) {
   return record(e);
 }
 
-// SWA_FWD_PER_HEAD=1 in the environment turns the GQA-packed forward off (every problem then
-// takes the per-head forward); read once.
+// SWA_FWD_PER_HEAD=1 in the environment turns the GQA-packed forward and dQ kernels off (every
+// problem then takes the per-head kernels); read once.
 bool gqa_forward_enabled() {
   static const bool on = [] {
     const char* v = getenv("SWA_FWD_PER_HEAD");
@@ -137,6 +138,11 @@ template <typename T, int D> struct Pre {
 };
 template <typename T, int D> struct Dq {
   static cudaError_t run(const swa::BwdParams& p, cudaStream_t s) {
+    if (gqa_forward_enabled()) {
+      bool used = false;
+      cudaError_t e = swa::launch_bwd_dq_gqa<T, D>(p, s, device_error_ptr(), &used);
+      if (used || e != cudaSuccess) return e;
+    }
     return swa::launch_bwd_dq_tc<T, D>(p, s, device_error_ptr());
   }
 };

@@ -75,14 +75,14 @@ inline bool make_tmap_2d(CUtensorMap* m, const void* base, int rows, int cols, i
 }
 
 // Tensor map over a row-major [rows, cols] fp32 matrix (row pitch `ld` elements, a multiple of
-// 4), no swizzle, box {box_cols, 1}.
+// 4), no swizzle, box {box_cols, box_rows}.
 inline bool make_tmap_rows_f32(CUtensorMap* m, const void* base, long long rows, int cols, int64_t ld,
-                               int box_cols) {
+                               int box_cols, int box_rows = 1) {
   EncodeTiledFn fn = encode_tiled_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
-  cuuint32_t box[2] = {(cuuint32_t)box_cols, 1};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box,
                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
