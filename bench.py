@@ -71,6 +71,8 @@ def kernel_work(w: wl.Workload, batch: int):
         "bwd_dkdv": dict(flops=8 * d * pairs, bytes=2 * qbytes + 2 * kbytes + 2 * rows + 2 * kbytes),
         # dQ pass: Q, dO, O, K, V, LSE read; dQ and Delta written
         "bwd_dq": dict(flops=6 * d * pairs, bytes=3 * qbytes + 2 * kbytes + 2 * rows + qbytes),
+        # whole backward (swa_bwd): Q, dO, O, K, V, LSE read once, dQ, dK, dV written once
+        "bwd": dict(flops=10 * d * pairs, bytes=3 * qbytes + 2 * kbytes + rows + qbytes + 2 * kbytes),
     }
 
 
@@ -183,7 +185,8 @@ def run_profile_phase(args, w, local_rank):
     plan = plan_mod.SwaPlan(q, k, v, w.window_size, w.sink_size, None, dout=do)
     for _ in range(args.warmup):
         plan.step()
-    fn = {"fwd": plan.fwd, "bwd_dq": plan.bwd_dq, "bwd_dkdv": plan.bwd_dkdv}[args.profile_phase]
+    fn = {"fwd": plan.fwd, "bwd": plan.bwd, "bwd_dq": plan.bwd_dq,
+          "bwd_dkdv": plan.bwd_dkdv}[args.profile_phase]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
@@ -218,8 +221,9 @@ def device_timed(w, dev, rank, steps, warmup):
     q, k, v, do = wl.make_inputs(w, device=dev)
     plan = plan_mod.SwaPlan(q, k, v, w.window_size, w.sink_size, None, dout=do)
     stream = torch.cuda.current_stream(dev)
-    phases = ("fwd", "bwd_dq", "bwd_dkdv")
-    fns = (plan.fwd, plan.bwd_dq, plan.bwd_dkdv)
+    # the backward as one call (swa_bwd: dQ, dK/dV and the sink-row reduction)
+    phases = ("fwd", "bwd")
+    fns = (plan.fwd, plan.bwd)
     for _ in range(warmup):
         plan.step(stream)
     torch.cuda.synchronize(dev)
@@ -714,7 +718,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-triton", action="store_true")
-    ap.add_argument("--profile-phase", choices=["fwd", "bwd_dq", "bwd_dkdv"], default=None,
+    ap.add_argument("--profile-phase", choices=["fwd", "bwd", "bwd_dq", "bwd_dkdv"], default=None,
                     help="profiling driver: `--warmup` full steps, then `--steps` launches of "
                          "this phase only (for an ncu capture with -k / -s / -c); prints one line")
     args = ap.parse_args()

@@ -27,7 +27,7 @@ SWA_BF16 = 1
 # Every extern "C" symbol include/swa_attn.h declares.
 EXPORTED_SYMBOLS = (
     "swa_fwd", "swa_bwd", "swa_bwd_preprocess", "swa_bwd_dq", "swa_bwd_dkdv",
-    "swa_bwd_workspace_size", "swa_bwd_dkdv_launch_count", "swa_bwd_no_alloc", "swa_check_device",
+    "swa_bwd_workspace_size", "swa_bwd_dkdv_launch_count", "swa_bwd_launch_count", "swa_bwd_no_alloc", "swa_check_device",
     "swa_status_string", "swa_last_cuda_error", "swa_version", "swa_lse_row_stride",
     "swa_selftest_wait_timeout", "swa_fwd_sink_logits", "swa_bwd_sink_logits",
     "swa_varlen_lse_floats", "swa_varlen_bwd_workspace_size", "swa_varlen_fwd", "swa_varlen_bwd",
@@ -127,8 +127,9 @@ def _declare(l):
     l.swa_varlen_bwd.restype = ctypes.c_int
     l.swa_bwd_workspace_size.argtypes = [P(SwaProblem)]
     l.swa_bwd_workspace_size.restype = ctypes.c_size_t
-    l.swa_bwd_dkdv_launch_count.argtypes = [P(SwaProblem)]
-    l.swa_bwd_dkdv_launch_count.restype = ctypes.c_int
+    for name in ("swa_bwd_dkdv_launch_count", "swa_bwd_launch_count"):
+        getattr(l, name).argtypes = [P(SwaProblem)]
+        getattr(l, name).restype = ctypes.c_int
     l.swa_check_device.argtypes = [ctypes.c_void_p]
     l.swa_check_device.restype = ctypes.c_int
     l.swa_status_string.argtypes = [ctypes.c_int]

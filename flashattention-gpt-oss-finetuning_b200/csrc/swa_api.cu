@@ -20,6 +20,7 @@ cudaError_t launch_sink_logit_grad(const float* lse, const float* delta, const f
 template <typename T, int D> cudaError_t launch_bwd_preprocess(const BwdParams&, cudaStream_t);
 template <typename T, int D> cudaError_t launch_bwd_dq_tc(const BwdParams&, cudaStream_t, int*);
 template <typename T, int D> cudaError_t launch_bwd_dq_gqa(const BwdParams&, cudaStream_t, int*, bool*);
+bool dq_gqa_covers(const BwdParams& p, int D);
 template <typename T, int D> cudaError_t launch_bwd_dkdv_tc(const BwdParams&, cudaStream_t, int*);
 }  // namespace swa
 
@@ -163,10 +164,46 @@ swa::SinkSplit split_of(const SwaProblem& p) {
                          p.n_kv_heads, p.head_dim);
 }
 
-size_t partial_bytes(const SwaProblem& p) {
+// Position tiles per work unit of the packed dQ kernel.
+constexpr int kDqUnit = 8;
+
+// Far sink pairs inside the packed dQ kernel: when the split sends them to the far sink-pair
+// kernel (one sink tile of at most 16 rows) and the packed dQ kernel takes the problem at
+// D = 64, swa_bwd lets the dQ kernel accumulate them instead ([Q^T; dO^T] [dS | P] on the
+// tensor cores, from tiles it has staged anyway) and leaves the far kernel out; the
+// partials then come one per dQ work unit.  Returns those units per (batch, KV head), 0 when
+// the fusion does not apply.
+int fused_far_units(const SwaProblem& p) {
+  if (check_problem(p) != SWA_OK || p.head_dim != 64 || !gqa_forward_enabled()) return 0;
   const swa::SinkSplit ss = split_of(p);
+  if (ss.fk_c <= 0 || ss.sp > 16 || ss.nst != 1) return 0;
+  swa::BwdParams kp = {};
+  kp.Hq = p.n_q_heads; kp.Hkv = p.n_kv_heads; kp.L = p.seq_len; kp.S = p.sink_size;
+  kp.W = effective_window(p.window_size, p.seq_len);
+  if (!swa::dq_gqa_covers(kp, 64)) return 0;
+  const int P = 128 / (p.n_q_heads / p.n_kv_heads);
+  // every far item (first row >= rfar) must hold the sink keys in its sink columns, i.e. its
+  // window box (ending at its last row) must start at or past key S
+  const int NW = ((kp.W > 0 ? kp.W : 1) + P - 1 + 15) / 16 * 16;
+  if (ss.rfar % P != 0 || ss.rfar + P - NW < p.sink_size) return 0;
+  const int n_pt = (p.seq_len + P - 1) / P;
+  return (n_pt + kDqUnit - 1) / kDqUnit;
+}
+
+size_t partial_bytes(const SwaProblem& p) {
+  swa::SinkSplit ss = split_of(p);
+  const int fu = fused_far_units(p);
+  if (fu > ss.fk_u && ss.fk_c > 0) ss.fk_u = fu;  // room for either way of computing them
   size_t n = (size_t)swa::sink_partial_floats(ss, p.batch, p.n_kv_heads, p.head_dim) * sizeof(float);
   return (n + 255) & ~(size_t)255;
+}
+
+// Switch a built launch plan to the fused far sink pairs (see fused_far_units).
+void fuse_far(const SwaProblem& p, swa::BwdParams* kp) {
+  const int fu = fused_far_units(p);
+  if (fu <= 0) return;
+  kp->far_in_dq = 1;
+  kp->fk_u = fu;
 }
 
 int build_bwd(const SwaBwdArgs* a, swa::BwdParams* kp) {
@@ -198,6 +235,8 @@ int build_bwd(const SwaBwdArgs* a, swa::BwdParams* kp) {
   kp->nst = ss.nst; kp->sp = ss.sp; kp->nc = ss.nc; kp->ch = ss.ch;
   kp->bn_split = ss.bn; kp->bm_split = ss.bm;
   kp->fk_c = ss.fk_c; kp->fk_u = ss.fk_u; kp->rfar = ss.rfar; kp->qf0 = ss.qf0; kp->nf = ss.nf;
+  kp->far_in_dq = 0;
+  kp->far_unit = kDqUnit;
   return SWA_OK;
 }
 
@@ -257,6 +296,13 @@ int swa_bwd_dkdv_launch_count(const SwaProblem* p) {
   if (!p || check_problem(*p) != SWA_OK || (int64_t)p->batch * p->seq_len == 0) return 0;
   const swa::SinkSplit ss = split_of(*p);
   return 1 + (ss.fk_c > 0 ? 1 : 0) + (ss.nst > 0 ? 1 : 0);
+}
+
+int swa_bwd_launch_count(const SwaProblem* p) {
+  if (!p || check_problem(*p) != SWA_OK || (int64_t)p->batch * p->seq_len == 0) return 0;
+  const swa::SinkSplit ss = split_of(*p);
+  const bool far_kernel = ss.fk_c > 0 && fused_far_units(*p) == 0;
+  return 2 + (far_kernel ? 1 : 0) + (ss.nst > 0 ? 1 : 0);
 }
 
 size_t swa_bwd_workspace_size(const SwaProblem* p) {
@@ -323,6 +369,7 @@ int swa_bwd(const SwaBwdArgs* a, void* stream) {
   int st = build_bwd(a, &kp);
   if (st || (int64_t)a->p.batch * a->p.seq_len == 0) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  fuse_far(a->p, &kp);
   // the dQ pass also computes Delta = rowsum(dO * O) into the workspace for the dK/dV pass
   if ((st = dispatch<Dq>(a->p, kp, s))) return st;
   return dispatch<Dkdv>(a->p, kp, s);
@@ -337,6 +384,7 @@ int swa_bwd_sink_logits(const SwaBwdArgs* a, const float* sink_logits, float* ds
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((int64_t)a->p.batch * a->p.seq_len != 0) {
     // the keys' gradients need no change: lse already holds the sink in each row's normaliser
+    fuse_far(a->p, &kp);
     if ((st = dispatch<Dq>(a->p, kp, s))) return st;
     if ((st = dispatch<Dkdv>(a->p, kp, s))) return st;
   }
@@ -537,8 +585,10 @@ int swa_varlen_bwd(const SwaVarlenBwdArgs* a, void* stream) {
     g.workspace_bytes = seq_ws_bytes(a->p, L);
     swa::BwdParams kp;
     const cudaStream_t si = fk.stream(i++);
-    if (!(st = build_bwd(&g, &kp)) && !(st = dispatch<Dq>(g.p, kp, si)))
-      st = dispatch<Dkdv>(g.p, kp, si);
+    if (!(st = build_bwd(&g, &kp))) {
+      fuse_far(g.p, &kp);
+      if (!(st = dispatch<Dq>(g.p, kp, si))) st = dispatch<Dkdv>(g.p, kp, si);
+    }
     lse_off += (size_t)a->p.n_q_heads * swa::stat_row_stride(L);
     ws_off += g.workspace_bytes;
   }

@@ -53,6 +53,36 @@ struct DqGqaGeom {
   int smem;
 };
 
+// Work units: U consecutive position tiles of one (b, KV head); CTAs take units in turn (CTAs
+// running at the same time work on neighbouring windows, which L2 then shares).  Walks this
+// CTA's items in order.
+struct UnitWalker {
+  int un, stride, n_units, n_ch, n_pt, U, Hkv;
+  int b, kvh, ch, pt, pt1;
+  __device__ void init(int first, int stride_, int n_units_, int n_ch_, int n_pt_, int U_, int Hkv_) {
+    stride = stride_; n_units = n_units_; n_ch = n_ch_; n_pt = n_pt_; U = U_; Hkv = Hkv_;
+    un = first - stride;
+    pt = pt1 = 0;
+  }
+  // Advance to the next item; false when there is none.
+  __device__ bool next() {
+    if (pt + 1 < pt1) {
+      ++pt;
+      return true;
+    }
+    un += stride;
+    if (un >= n_units) return false;
+    ch = un % n_ch;
+    const int rest = un / n_ch;
+    kvh = rest % Hkv;
+    b = rest / Hkv;
+    pt = ch * U;
+    pt1 = min(n_pt, pt + U);
+    return true;
+  }
+  __device__ bool last_in_unit() const { return pt + 1 == pt1; }
+};
+
 template <int D>
 struct DqGqaCfg {
   static_assert(D <= 64, "the packed dQ kernel covers head dims up to 64");
@@ -61,6 +91,10 @@ struct DqGqaCfg {
   static constexpr int T_BYTES = 128 * D * 2;  // a Q, dO, O or dQ tile
   static constexpr int NST = 2;
   static constexpr int S_COL = 0, DP_COL = 160, DS_COL = 320, DQ_COL = 400;
+  // far sink pairs: [dS | P] of the sink columns (16 each) staged MN-major, 64-byte rows, and
+  // the accumulator [Q^T; dO^T] [dS | P] (M = 128, N = 32)
+  static constexpr int FS_BYTES = 128 * 64;
+  static constexpr int ACC_COL = 464;
   static constexpr int SMEM_LIMIT = 227 * 1024;
 };
 
@@ -76,11 +110,12 @@ __global__ void __launch_bounds__(128 * NC + 224, 1)
   constexpr int MMA_Q = PROD + 2;    // dQ issuer
   constexpr int NEL = 128 * NC;      // elementwise threads
   extern __shared__ unsigned char smem_raw[];
-  // [NST stages: Q, dO, O, K, V, LSE] [2 dQ staging tiles] [Delta: NST x 128]
+  // [NST stages: Q, dO, O, K, V, LSE] [2 dQ staging tiles] [Delta: NST x 128] [far staging]
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* Qst = smem + C::NST * gm.stage_bytes;
   float* dsm = reinterpret_cast<float*>(Qst + 2 * C::T_BYTES);
+  unsigned char* Fst = reinterpret_cast<unsigned char*>(dsm + C::NST * 128);  // 1024-aligned
   const int kv_bytes = gm.N * C::ROWB;
   auto st_q = [&](int s) { return smem + s * gm.stage_bytes; };
   auto st_do = [&](int s) { return st_q(s) + C::T_BYTES; };
@@ -91,6 +126,7 @@ __global__ void __launch_bounds__(128 * NC + 224, 1)
 
   __shared__ uint64_t bar_full[C::NST], bar_empty[C::NST], bar_delta[C::NST];
   __shared__ uint64_t bar_sdp, bar_sdp_free, bar_ds, bar_ds_free, bar_dq, bar_dq_free;
+  __shared__ uint64_t bar_acc, bar_acc_free;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
 
@@ -114,6 +150,8 @@ __global__ void __launch_bounds__(128 * NC + 224, 1)
     mbar_init(&bar_ds_free, 1);
     mbar_init(&bar_dq, 1);
     mbar_init(&bar_dq_free, 128);
+    mbar_init(&bar_acc, 1);
+    mbar_init(&bar_acc_free, 128);
     fence_mbar_init();
   }
   if (warp == PROD) {
@@ -127,15 +165,23 @@ __global__ void __launch_bounds__(128 * NC + 224, 1)
   pdl_wait();
   pdl_trigger();
 
-  auto decode = [&](int it, int* b, int* kvh, int* pt) {
-    *pt = it % n_pt;
-    const int rest = it / n_pt;
-    *kvh = rest % Hkv;
-    *b = rest / Hkv;
-  };
   auto win_start = [&](int q0) { return max(0, q0 + P - NW); };
+  const int U = p.far_unit;
+  const int n_ch = (n_pt + U - 1) / U;
+  const int n_units = p.B * Hkv * n_ch;
+  auto walker = [&]() {
+    UnitWalker w;
+    w.init(blockIdx.x, gridDim.x, n_units, n_ch, n_pt, U, Hkv);
+    return w;
+  };
   int n_mine = 0;
-  for (int it = blockIdx.x; it < n_items; it += gridDim.x) ++n_mine;
+  {
+    UnitWalker w = walker();
+    while (w.next()) ++n_mine;
+  }
+  // far sink pairs of item (q0 >= rfar): every row sees the sink keys through the sink rule only
+  auto is_far = [&](int pt) { return p.far_in_dq != 0 && pt * P >= p.rfar; };
+  (void)n_items;
 
   if (warp == PROD) {
     // ------------------------------------------------------------------ TMA producer
@@ -143,9 +189,10 @@ __global__ void __launch_bounds__(128 * NC + 224, 1)
       tma_prefetch_desc(&tm.q);
       tma_prefetch_desc(&tm.k);
       bool ok = true;
+      UnitWalker wk = walker();
       for (int k = 0; k < n_mine && ok; ++k) {
-        int b, kvh, pt;
-        decode(blockIdx.x + k * gridDim.x, &b, &kvh, &pt);
+        wk.next();
+        const int b = wk.b, kvh = wk.kvh, pt = wk.pt;
         const int q0 = pt * P, key0 = win_start(q0);
         const int s = k % C::NST;
         if (k >= C::NST && !(ok = mbar_wait(&bar_empty[s], ((k / C::NST) - 1) & 1, &abort_sh))) break;
@@ -195,8 +242,13 @@ __global__ void __launch_bounds__(128 * NC + 224, 1)
     // ------------------------------------------------------------------ dQ issuer
     if (lane == 0 && !dead) {
       constexpr uint32_t id_q = idesc_f16(128, D, kBf16, false, true);
+      constexpr uint32_t id_acc = idesc_f16(128, 32, kBf16, true, true);
       bool ok = true;
+      UnitWalker wk = walker();
+      int acc_n = 0;        // far units accumulated so far
+      bool acc_on = false;  // this unit has accumulated a far item
       for (int k = 0; k < n_mine && ok; ++k) {
+        wk.next();
         const int s = k % C::NST;
         if (!(ok = mbar_wait(&bar_ds, k & 1, &abort_sh))) break;
         // the epilogue has read item k - 1's dQ
@@ -206,9 +258,28 @@ __global__ void __launch_bounds__(128 * NC + 224, 1)
         for (int ks = 0; ks < N / 16; ++ks)
           mma_ts(tmem + C::DQ_COL, tmem + C::DS_COL + ks * 8, sdesc_add(kmn, ks * 16 * C::ROWB), id_q,
                  ks > 0 ? 1u : 0u);
+        if (is_far(wk.pt)) {
+          // the sink keys' dK^T, dV^T += [Q^T; dO^T] [dS | P] over this item's 128 rows; the
+          // first far item of a unit starts from zero once the epilogue has read the last
+          // unit's accumulator
+          if (!acc_on && acc_n > 0 && !(ok = mbar_wait(&bar_acc_free, (acc_n - 1) & 1, &abort_sh))) break;
+          tc_fence_after();
+          const uint64_t qa = sdesc(saddr(st_q(s)), C::T_BYTES, 8 * C::ROWB, C::SWZ);  // Q^T, dO^T
+          const uint64_t fb = sdesc(saddr(Fst), 512, 512, kSw64);                      // [dS | P]
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            mma_ss(tmem + C::ACC_COL, sdesc_add(qa, ks * 16 * C::ROWB), sdesc_add(fb, ks * 1024), id_acc,
+                   (acc_on || ks > 0) ? 1u : 0u);
+          acc_on = true;
+        }
         mma_commit(&bar_empty[s]);
         mma_commit(&bar_ds_free);
         mma_commit(&bar_dq);
+        if (wk.last_in_unit() && acc_on) {
+          mma_commit(&bar_acc);
+          ++acc_n;
+          acc_on = false;
+        }
       }
       if (!ok) {
         abort_sh = 1;
@@ -223,9 +294,13 @@ __global__ void __launch_bounds__(128 * NC + 224, 1)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     constexpr uint32_t SWM = C::ROWB / 16 - 1;  // swizzle: 16-byte unit ^= (offset >> 7) & SWM
     bool ok = !dead;
+    UnitWalker wd = walker();  // items whose Delta is formed (one ahead)
+    UnitWalker wq = walker();  // items whose dQ is written
+    int acc_e = 0;             // far units read out so far
     // Delta = rowsum(dO * O) of item j from its staged tiles: to shared memory for the
     // elementwise threads and to the workspace for the dK / dV pass
     auto delta = [&](int j) {
+      wd.next();
       const int s = j % C::NST;
       if (ok) ok = mbar_wait(&bar_full[s], (j / C::NST) & 1, &abort_sh);
       float acc = 0.f;
@@ -242,8 +317,7 @@ __global__ void __launch_bounds__(128 * NC + 224, 1)
           for (int e = 0; e < 8; ++e) acc = fmaf(Pack<T>::to(de[e]), Pack<T>::to(oe[e]), acc);
         }
       }
-      int b, kvh, pt;
-      decode(blockIdx.x + j * gridDim.x, &b, &kvh, &pt);
+      const int b = wd.b, kvh = wd.kvh, pt = wd.pt;
       const int i = pt * P + pos;
       dsm[s * 128 + r] = i < L ? acc : 0.f;
       float* drow = p.delta + ((int64_t)b * Hq + kvh * G + g) * p.lse_ld;
@@ -258,8 +332,8 @@ __global__ void __launch_bounds__(128 * NC + 224, 1)
       if (ok) ok = mbar_wait(&bar_dq, k & 1, &abort_sh);
       if (!ok) break;
       tc_fence_after();
-      int b, kvh, pt;
-      decode(blockIdx.x + k * gridDim.x, &b, &kvh, &pt);
+      wq.next();
+      const int b = wq.b, kvh = wq.kvh, pt = wq.pt;
       unsigned char* Qs = Qst + (k & 1) * C::T_BYTES;
       if (r == 0) bulk_wait_read_all();  // the store of item k - 2 has read this tile
       named_bar_sync(1, 128);
@@ -291,6 +365,28 @@ __global__ void __launch_bounds__(128 * NC + 224, 1)
         tma_store_4d(&tm.dq, Qs, 0, pt * P, kvh * G, b);
         bulk_commit();
       }
+      if (p.far_in_dq && wq.last_in_unit()) {
+        // partial slot 1 + unit of the sink-row reduction: lane m < 64 holds dK_s^T row d = m
+        // (columns 0..15), lane 64 + d holds dV_s^T row d (columns 16..31); a unit with no far
+        // item writes zeros
+        const bool had = is_far(pt);
+        float* part = p.part + (((int64_t)(1 + wq.ch) * p.B + b) * p.Hkv + kvh) * 2 * p.sp * D +
+                      (int64_t)(r >> 6) * p.sp * D + (r & 63);
+        const bool dv_row = r >= 64;  // warp-uniform (lane quadrants 2, 3)
+        uint32_t v[16];
+        if (had) {
+          if (!(ok = mbar_wait(&bar_acc, acc_e & 1, &abort_sh))) break;
+          tc_fence_after();
+          tmem_ld16(tmem + C::ACC_COL + (dv_row ? 16 : 0) + lane_off, v);
+          tmem_ld_wait();
+          tc_fence_before();
+          mbar_arrive(&bar_acc_free);
+          ++acc_e;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (j < p.sp) part[(int64_t)j * D] = had ? __uint_as_float(v[j]) : 0.f;
+      }
     }
     if (r == 0) bulk_wait_all();
     if (!ok && !dead) {
@@ -308,11 +404,13 @@ __global__ void __launch_bounds__(128 * NC + 224, 1)
     const int c0 = grp * 32;
     const bool ctail = grp == NC - 1 && (N & 31) != 0;  // this chunk holds 16 columns
     bool ok = !dead;
+    UnitWalker wk = walker();
     for (int k = 0; k < n_mine && ok; ++k) {
+      wk.next();
       const int s = k % C::NST;
-      int b, kvh, pt;
-      decode(blockIdx.x + k * gridDim.x, &b, &kvh, &pt);
+      const int pt = wk.pt;
       const int q0 = pt * P, key0 = win_start(q0);
+      const bool stage_far = grp == 0 && is_far(pt);  // stage [dS | P] of the sink columns
       const int i = q0 + pos;
       const int smax = min(S, key0);  // sink keys outside the window box
       if (!(ok = mbar_wait(&bar_sdp, k & 1, &abort_sh))) break;
@@ -333,7 +431,7 @@ __global__ void __launch_bounds__(128 * NC + 224, 1)
       }
       const float2 sl2v = make_float2(sl2, sl2), nlse = make_float2(-lse_r, -lse_r);
       const float2 ndl = make_float2(-dl_r, -dl_r);
-      uint32_t dw[16];
+      uint32_t dw[16], pw[8];
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
         if (h2 == 1 && ctail) {
@@ -355,18 +453,34 @@ __global__ void __launch_bounds__(128 * NC + 224, 1)
           const float2 t = __ffma2_rn(make_float2(sv[2 * e], sv[2 * e + 1]), sl2v, nlse);
           const float2 pr = make_float2(fast_exp2(t.x), fast_exp2(t.y));
           float2 ds = __fmul2_rn(pr, __fadd2_rn(make_float2(dp[2 * e], dp[2 * e + 1]), ndl));
+          float2 pv = pr;
           if (!full) {
             const int bit = 16 * h2 + 2 * e;
             ds.x = (vm & (1u << bit)) ? ds.x : 0.f;
             ds.y = (vm & (2u << bit)) ? ds.y : 0.f;
+            pv.x = (vm & (1u << bit)) ? pv.x : 0.f;
+            pv.y = (vm & (2u << bit)) ? pv.y : 0.f;
           }
           dw[8 * h2 + e] = Pack<T>::pack(ds.x, ds.y);
+          if (h2 == 0) pw[e] = Pack<T>::pack(pv.x, pv.y);
         }
       }
       // dS of item k - 1 has been read by its dQ MMAs
       if (k >= 1 && !(ok = mbar_wait(&bar_ds_free, (k - 1) & 1, &abort_sh))) break;
       tc_fence_after();
       tmem_st16(tmem + C::DS_COL + grp * 16 + lane_off, dw);
+      if (stage_far) {
+        // row r of the staging tile: dS of sink columns 0..15 in 16-byte units 0, 1, P in 2, 3
+        // (64-byte swizzle, as the MMA's MN-major B operand reads it)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint32_t off = r * 64 + u * 16;
+          off ^= ((off >> 7) & 3u) << 4;
+          const uint32_t* src = u < 2 ? dw + 4 * u : pw + 4 * (u - 2);
+          *reinterpret_cast<uint4*>(Fst + off) = make_uint4(src[0], src[1], src[2], src[3]);
+        }
+        fence_proxy_async_smem();  // generic-proxy writes before the MMAs read them
+      }
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&bar_ds);
@@ -397,8 +511,19 @@ bool dq_gqa_geometry(const BwdParams& p, DqGqaGeom* gm) {
   gm->N = gm->SB + gm->NW;
   if (gm->N > 160) return false;  // S and dP side by side, dS and dQ after them
   gm->stage_bytes = (3 * C::T_BYTES + 2 * gm->N * C::ROWB + 128 * 4 + 1023) / 1024 * 1024;
-  gm->smem = 1024 + C::NST * gm->stage_bytes + 2 * C::T_BYTES + C::NST * 128 * 4;
+  gm->smem = 1024 + C::NST * gm->stage_bytes + 2 * C::T_BYTES + 1024 + C::FS_BYTES;
   return gm->smem <= C::SMEM_LIMIT;
+}
+
+// Whether the packed dQ kernel takes this problem (host side, for the launch plan).
+bool dq_gqa_covers(const BwdParams& p, int D) {
+  DqGqaGeom gm;
+  switch (D) {
+    case 16: return dq_gqa_geometry<16>(p, &gm);
+    case 32: return dq_gqa_geometry<32>(p, &gm);
+    case 64: return dq_gqa_geometry<64>(p, &gm);
+    default: return false;
+  }
 }
 
 template <typename T, int D>

@@ -543,7 +543,8 @@ cudaError_t launch_bwd_dkdv_tc(const BwdParams& p, cudaStream_t st, int* err) {
   if (grid <= 0) return cudaErrorInvalidConfiguration;
   e = launch_pdl(kern, grid, C::THREADS, C::SMEM, st, tm, p, err);
   if (e != cudaSuccess || p.nst == 0) return e;
-  if (p.fk_c > 0 && (e = launch_sink_far<T, D>(p, st, err)) != cudaSuccess) return e;
+  // far sink pairs: their own kernel, unless the dQ pass has accumulated them (far_in_dq)
+  if (p.fk_c > 0 && !p.far_in_dq && (e = launch_sink_far<T, D>(p, st, err)) != cudaSuccess) return e;
   return launch_sink_reduce<T, D>(p, st);
 }
 

@@ -43,6 +43,10 @@ struct BwdParams {
   int nst, sp, nc, ch;  // SinkSplit
   int bn_split, bm_split;  // key / query tile sizes the split was made for
   int fk_c, fk_u, rfar, qf0, nf;  // SinkSplit far-pair kernel fields (fk_c = 0: not used)
+  int far_in_dq;   // 1: the packed dQ kernel writes the far sink-pair partials (slots 1 ..
+                   // fk_u, one per unit of far_unit position tiles) and the dK/dV launch
+                   // sequence leaves out the far sink-pair kernel
+  int far_unit;    // position tiles per dQ work unit
 };
 
 }  // namespace swa

@@ -51,8 +51,10 @@ class SwaPlan:
         self._ba = ctypes.byref(self.bwd_args)
         self.device = q.device
         self.launches = 0
-        # swa_bwd_dkdv also launches the far sink-pair kernel and the sink-row reduction
+        # swa_bwd_dkdv also launches the far sink-pair kernel and the sink-row reduction;
+        # swa_bwd may fold the far sink pairs into its dQ kernel
         self._dkdv_kernels = self.lib.swa_bwd_dkdv_launch_count(ctypes.byref(self.problem))
+        self._bwd_kernels = self.lib.swa_bwd_launch_count(ctypes.byref(self.problem))
 
     def _s(self, stream) -> int:
         return (stream or torch.cuda.current_stream(self.device)).cuda_stream
@@ -74,9 +76,10 @@ class SwaPlan:
         self.launches += 1
 
     def bwd(self, stream=None):
-        """dQ (which also writes Delta to the workspace), then dK / dV."""
-        self.bwd_dq(stream)
-        self.bwd_dkdv(stream)
+        """The whole backward (swa_bwd): dQ (which also writes Delta to the workspace), then
+        dK / dV."""
+        _lib.check(self.lib.swa_bwd(self._ba, self._s(stream)), "swa_bwd")
+        self.launches += self._bwd_kernels
 
     def step(self, stream=None):
         """One forward + backward over the bound buffers.  Raises SwaDeviceTimeout when an

@@ -106,8 +106,14 @@ SWA_API size_t swa_bwd_workspace_size(const SwaProblem* p);
 SWA_API int swa_bwd_dkdv_launch_count(const SwaProblem* p);
 
 /* Full backward: dQ (which also writes Delta) then dK/dV.  Replaces
- * flash_attention_gpt_oss.py:397-435. */
+ * flash_attention_gpt_oss.py:397-435.  Where the GQA-packed dQ kernel takes the problem and
+ * the sink keys' contributions from rows far past their window are few (one sink tile of at
+ * most 16 keys, head dim 64), the dQ kernel also accumulates those contributions, so the
+ * sequence launches one kernel fewer than swa_bwd_dq followed by swa_bwd_dkdv. */
 SWA_API int swa_bwd(const SwaBwdArgs* args, void* stream);
+
+/* Kernels swa_bwd launches for this problem (0 for an invalid or empty problem). */
+SWA_API int swa_bwd_launch_count(const SwaProblem* p);
 
 /* Delta[b,h,i] = sum_d dout * o, written to the front of the workspace (stand-alone; swa_bwd
  * and swa_bwd_dq compute it inside the dQ pass).  Replaces flash_attention_gpt_oss.py:403. */
