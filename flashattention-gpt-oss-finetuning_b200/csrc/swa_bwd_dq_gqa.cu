@@ -373,19 +373,24 @@ __global__ void __launch_bounds__(128 * NC + 224, 1)
         float* part = p.part + (((int64_t)(1 + wq.ch) * p.B + b) * p.Hkv + kvh) * 2 * p.sp * D +
                       (int64_t)(r >> 6) * p.sp * D + (r & 63);
         const bool dv_row = r >= 64;  // warp-uniform (lane quadrants 2, 3)
-        uint32_t v[16];
+        if (had && !(ok = mbar_wait(&bar_acc, acc_e & 1, &abort_sh))) break;
+        if (had) tc_fence_after();
+#pragma unroll 1
+        for (int j0 = 0; j0 < p.sp; j0 += 8) {
+          uint32_t v[8];
+          if (had) {
+            tmem_ld8(tmem + C::ACC_COL + (dv_row ? 16 : 0) + j0 + lane_off, v);
+            tmem_ld_wait();
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (j0 + j < p.sp) part[(int64_t)(j0 + j) * D] = had ? __uint_as_float(v[j]) : 0.f;
+        }
         if (had) {
-          if (!(ok = mbar_wait(&bar_acc, acc_e & 1, &abort_sh))) break;
-          tc_fence_after();
-          tmem_ld16(tmem + C::ACC_COL + (dv_row ? 16 : 0) + lane_off, v);
-          tmem_ld_wait();
           tc_fence_before();
           mbar_arrive(&bar_acc_free);
           ++acc_e;
         }
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (j < p.sp) part[(int64_t)j * D] = had ? __uint_as_float(v[j]) : 0.f;
       }
     }
     if (r == 0) bulk_wait_all();
