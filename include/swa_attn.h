@@ -217,7 +217,11 @@ SWA_API int swa_varlen_bwd(const SwaVarlenBwdArgs* args, void* stream);
 #define SWA_NO_ALLOC_SCRATCH_BYTES ((size_t)16 << 20)
 SWA_API int swa_bwd_no_alloc(const SwaBwdArgs* args, void* stream);
 
-/* Synchronise `stream`, then report (and clear) the current device's on-device error flag:
+/* (Every entry point: the library caches per device ordinal the addresses of its device-side
+ * flag and scratch arrays for the life of the process, so it must not outlive a reset of the
+ * device or of its primary context.)
+ *
+ * Synchronise `stream`, then report (and clear) the current device's on-device error flag:
  * SWA_ERR_DEVICE_TIMEOUT if a bounded wait inside a kernel gave up since the last check
  * (that launch's outputs are then undefined), SWA_OK otherwise. */
 SWA_API int swa_check_device(void* stream);
