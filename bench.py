@@ -689,7 +689,11 @@ def run_variant(args, w, local_rank):
 # per step of a phase, from one ncu capture of `bench.py --steps 1 --warmup 3`, keyed by
 # (hash of the kernel sources, workload, phase).  A figure taken on other kernel sources is
 # never reported: the line then carries traffic = null.
-TRAFFIC: dict = {}
+TRAFFIC: dict = {
+    # bwd = bwd_dq_gqa 560.7 MB + bwd_dkdv 345.2 MB + bwd_sink_reduce 2.2 MB; fwd = fwd_gqa
+    ("6bc957277f57", "cfg2_gptoss_swa", "bwd"): 560_742_400 + 345_186_490 + 2_174_999,
+    ("6bc957277f57", "cfg2_gptoss_swa", "fwd"): 262_824_308,
+}
 
 
 def kernel_sources_sha() -> str:
