@@ -167,7 +167,7 @@ def run_reference(args, w, rank, world):
     line = {
         "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT,
         "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
-        "ms_per_step": cb["ms_per_sample"], "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": cb["ms_per_sample"], "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded randn, BASELINE shapes)",
         "config": dict(w.describe(), sample="1 (batch, query head) slice per step"),
         "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
